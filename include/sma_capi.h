@@ -1,0 +1,113 @@
+/*
+ * sma_capi.h - C ABI of the B200 sparse-mask attention library (libsma.so).
+ *
+ * Plain pointers and sizes only: every tensor argument is a device pointer to
+ * a contiguous row-major buffer, every stream argument is a cudaStream_t passed
+ * as void* (NULL = legacy default stream).  Work is enqueued asynchronously on
+ * that stream; nothing synchronises except sma_device_status().
+ *
+ * Every function returns an SMA_* status.  On a non-zero status,
+ * sma_last_error() returns a message describing the failure (thread-local,
+ * valid until the next call on the same thread).
+ *
+ * Each entry point names the reference interface it replaces
+ * (yulangz/sparse-mask-attention-auto-research, paths relative to its root).
+ */
+#ifndef SMA_CAPI_H_
+#define SMA_CAPI_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. */
+#define SMA_OK 0
+#define SMA_ERR_ARG 1             /* bad pointer / size / layout argument          */
+#define SMA_ERR_DTYPE 2           /* dtype is neither fp16 nor bf16                 */
+#define SMA_ERR_UNSUPPORTED_D 3   /* head dim other than 64 or 128                  */
+#define SMA_ERR_LAUNCH 4          /* kernel launch failed                           */
+#define SMA_ERR_TIMEOUT 5         /* a device-side wait gave up (see sma_device_status) */
+#define SMA_ERR_UNSUPPORTED_N 6   /* sequence length above SMA_MAX_SEQ_LEN          */
+#define SMA_ERR_CUDA 7            /* CUDA runtime / driver error                    */
+
+/* Element types of q, k, v and out. */
+#define SMA_DTYPE_FP16 0
+#define SMA_DTYPE_BF16 1
+
+#define SMA_MAX_SEQ_LEN 8192
+
+#if defined(__GNUC__)
+#define SMA_API __attribute__((visibility("default")))
+#else
+#define SMA_API
+#endif
+#define SMA_ABI_VERSION 1
+
+/*
+ * Pack a bool mask [B, H, N, N] (one byte per element, non-zero = attend)
+ * into 32-bit words [B, H, N, ceil(N/32)]: bit b of word w of a row is the
+ * mask at column 32*w + b; bits at columns >= N are zero.  The output has the
+ * bit pattern of the reference's int32 packed tensor.
+ *
+ * Replaces: pack_mask()            csrc/binding.cpp:49-66
+ *           pack_mask_bits()       csrc/sparse_attention.cu:44-54
+ *           (CPU fallback          python/sparse_attention.py:189-206)
+ * Unlike the reference binding, the caller allocates `packed`.
+ */
+SMA_API int sma_pack_mask(const void* mask, void* packed, int64_t B, int64_t H, int64_t N, void* stream);
+
+/*
+ * Masked-softmax attention forward:
+ *   out[b,h,i,:] = sum_j softmax_j(scale * q_i . k_j  over j with bit(i,j) set) * v[b,h,j,:]
+ * q, k, v, out: [B, H, N, D] of `dtype`; mask_packed: [B, H, N, ceil(N/32)]
+ * words as produced by sma_pack_mask; lse: [B, H, N] float32 log-sum-exp of
+ * the scaled scores, or NULL to skip it (the reference's is_training=false).
+ * Rows with no set bit get out = 0 and lse = -FLT_MAX (the reference CUDA
+ * convention, csrc/sparse_attention.cu:133,141).
+ * Supported: D in {64, 128}, 1 <= N <= SMA_MAX_SEQ_LEN, 16-byte aligned
+ * q/k/v/out.
+ *
+ * Replaces: forward()                          csrc/binding.cpp:9-47
+ *           sparse_attention_fwd_fp16/_bf16()  csrc/sparse_attention.cu:149-185
+ *           SparseAttentionParams              csrc/sparse_attention.h:12-38
+ */
+SMA_API int sma_attn_fwd(int dtype, const void* q, const void* k, const void* v, const void* mask_packed,
+                 void* out, float* lse, int64_t B, int64_t H, int64_t N, int64_t D, float scale,
+                 void* stream);
+
+/*
+ * Synchronise `stream`, then report whether any kernel of this library on the
+ * current device gave up a bounded device-side wait since the last clear
+ * (SMA_ERR_TIMEOUT), or whether the stream holds a CUDA error (SMA_ERR_CUDA).
+ * clear != 0 resets the device error word.
+ * No reference counterpart (the reference never checks its launches).
+ */
+SMA_API int sma_device_status(void* stream, int clear);
+
+/*
+ * Upper bound, in nanoseconds, of every device-side wait in later launches
+ * (default 2e9).  No reference counterpart.
+ */
+SMA_API int sma_set_wait_timeout_ns(uint64_t ns);
+
+/*
+ * Launch a one-CTA kernel that waits, through the library's bounded-wait
+ * helper, on a barrier nothing ever signals; it gives up after timeout_ns and
+ * raises the device error word.  Used to test failure reporting without
+ * faulting or hanging a GPU.  No reference counterpart.
+ */
+SMA_API int sma_debug_wait_probe(uint64_t timeout_ns, void* stream);
+
+/* Thread-local message for the last non-zero status. */
+SMA_API const char* sma_last_error(void);
+
+/* SMA_ABI_VERSION of the loaded library. */
+SMA_API int sma_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SMA_CAPI_H_ */

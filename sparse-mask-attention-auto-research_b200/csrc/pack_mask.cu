@@ -1,0 +1,121 @@
+// bool [rows, N] -> uint32 [rows, ceil(N/32)] bit packing.
+//
+// Semantics follow the reference packer (python/sparse_attention.py:189-206,
+// csrc/sparse_attention.cu:20-42): bit b of word w of a row is set iff the
+// mask byte at column 32*w + b is true (non-zero); bits at columns >= N are 0.
+//
+// Layout in HBM: the input is B*H*N rows of N bytes, the output B*H*N rows of
+// ceil(N/32) words, both row-major and contiguous.  The kernel is purely
+// HBM-bound (N^2 bytes read and N^2/8 written per head), so the design goal
+// is fully coalesced 16-byte loads and 4-byte stores with enough bytes in
+// flight per SM, not arithmetic.
+//
+// Fast path (N % 32 == 0 and 16-byte aligned input): every output word is one
+// aligned 32-byte chunk of the flat input, independent of row boundaries.  A
+// warp packs 32 consecutive words per round (1 KiB of input), four rounds per
+// thread with all eight 16-byte loads issued before any use.
+// General path: one thread per output word with byte loads (any N, any
+// alignment).
+#include "sma_internal.h"
+
+namespace sma {
+namespace {
+
+// 4 mask bytes -> 4 bits (byte k -> bit k), treating any non-zero byte as set.
+__device__ __forceinline__ uint32_t pack4(uint32_t x) {
+  // High bit of each byte := byte != 0 (no carries cross byte lanes).
+  uint32_t hi = (((x & 0x7F7F7F7Fu) + 0x7F7F7F7Fu) | x) & 0x80808080u;
+  // Gather the four high bits into bits 28..31 with one multiply.
+  return (hi * 0x00204081u) >> 28;
+}
+
+__device__ __forceinline__ uint32_t pack16(uint4 v) {
+  return pack4(v.x) | (pack4(v.y) << 4) | (pack4(v.z) << 8) | (pack4(v.w) << 12);
+}
+
+constexpr int kPackThreads = 256;
+constexpr int kPackRounds = 4;
+
+__global__ void __launch_bounds__(kPackThreads) pack_mask_aligned_kernel(
+    const uint4* __restrict__ in, uint32_t* __restrict__ out, int64_t total_words) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp_global = (static_cast<int64_t>(blockIdx.x) * kPackThreads + threadIdx.x) >> 5;
+  const int64_t base = warp_global * (32 * kPackRounds);
+  uint4 lo[kPackRounds], hi[kPackRounds];
+#pragma unroll
+  for (int r = 0; r < kPackRounds; ++r) {
+    const int64_t w = base + r * 32 + lane;
+    if (w < total_words) {
+      lo[r] = __ldcs(in + 2 * w);
+      hi[r] = __ldcs(in + 2 * w + 1);
+    } else {
+      lo[r] = make_uint4(0, 0, 0, 0);
+      hi[r] = lo[r];
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < kPackRounds; ++r) {
+    const int64_t w = base + r * 32 + lane;
+    if (w < total_words) out[w] = pack16(lo[r]) | (pack16(hi[r]) << 16);
+  }
+}
+
+__global__ void __launch_bounds__(kPackThreads) pack_mask_generic_kernel(
+    const uint8_t* __restrict__ in, uint32_t* __restrict__ out, int64_t rows, int64_t n,
+    int64_t n_words) {
+  const int64_t idx = static_cast<int64_t>(blockIdx.x) * kPackThreads + threadIdx.x;
+  if (idx >= rows * n_words) return;
+  const int64_t row = idx / n_words;
+  const int64_t w = idx - row * n_words;
+  const uint8_t* src = in + row * n + w * 32;
+  const int64_t cols = (n - w * 32) < 32 ? (n - w * 32) : 32;
+  uint32_t bits = 0;
+  for (int b = 0; b < cols; ++b) bits |= static_cast<uint32_t>(src[b] != 0) << b;
+  out[idx] = bits;
+}
+
+}  // namespace
+
+int launch_pack_mask(const uint8_t* mask, uint32_t* packed, int64_t rows, int64_t n,
+                     cudaStream_t stream, const char** msg) {
+  if (rows < 0 || n < 0) {
+    *msg = "pack_mask: negative size";
+    return kErrArg;
+  }
+  if (rows == 0 || n == 0) return kOk;
+  if (mask == nullptr || packed == nullptr) {
+    *msg = "pack_mask: null pointer";
+    return kErrArg;
+  }
+  const int64_t n_words = (n + 31) / 32;
+  const bool aligned = (n % 32 == 0) && (reinterpret_cast<uintptr_t>(mask) % 16 == 0) &&
+                       (reinterpret_cast<uintptr_t>(packed) % 4 == 0);
+  if (aligned) {
+    const int64_t total_words = rows * n_words;
+    const int64_t words_per_block = (kPackThreads / 32) * 32 * kPackRounds;
+    const int64_t blocks = (total_words + words_per_block - 1) / words_per_block;
+    if (blocks > 0x7FFFFFFFll) {
+      *msg = "pack_mask: input too large";
+      return kErrArg;
+    }
+    pack_mask_aligned_kernel<<<static_cast<unsigned>(blocks), kPackThreads, 0, stream>>>(
+        reinterpret_cast<const uint4*>(mask), packed, total_words);
+  } else {
+    const int64_t total = rows * n_words;
+    const int64_t blocks = (total + kPackThreads - 1) / kPackThreads;
+    if (blocks > 0x7FFFFFFFll) {
+      *msg = "pack_mask: input too large";
+      return kErrArg;
+    }
+    pack_mask_generic_kernel<<<static_cast<unsigned>(blocks), kPackThreads, 0, stream>>>(
+        mask, packed, rows, n, n_words);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    *msg = cudaGetErrorString(e);
+    return kErrLaunch;
+  }
+  return kOk;
+}
+
+}  // namespace sma

@@ -1,0 +1,142 @@
+// C-ABI layer of libsma.so: argument validation, dispatch to the kernel
+// launchers, the thread-local error message, and the device error word the
+// kernels raise when a bounded wait gives up.
+//
+// Mirrors the reference pybind layer (csrc/binding.cpp:9-71), whose checks
+// (CUDA tensors, 4-D shapes, fp16/bf16 dtype) become SMA_* status codes here;
+// the Python shim turns them into RuntimeError like TORCH_CHECK does.
+#include <cstdio>
+#include <string>
+
+#include "sma_capi.h"
+#include "sma_internal.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+uint64_t g_timeout_ns = 2000000000ull;
+
+// Device word the kernels OR error bits into (one instance per device).
+__device__ uint32_t g_device_error_word;
+
+constexpr int kMaxDevices = 64;
+uint32_t* g_err_ptr[kMaxDevices] = {};
+
+int fail(int code, const char* msg) {
+  g_last_error = msg ? msg : "unknown error";
+  return code;
+}
+
+int fail_cuda(cudaError_t e, const char* where) {
+  g_last_error = std::string(where) + ": " + cudaGetErrorString(e);
+  return sma::kErrCuda;
+}
+
+// Device address of the error word on the current device.
+int error_word(uint32_t** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(sma::kErrCuda, "device index out of range");
+  if (g_err_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_device_error_word);
+    if (e != cudaSuccess) return fail_cuda(e, "cudaGetSymbolAddress");
+    g_err_ptr[dev] = static_cast<uint32_t*>(p);
+  }
+  *out = g_err_ptr[dev];
+  return sma::kOk;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+int sma_pack_mask(const void* mask, void* packed, int64_t B, int64_t H, int64_t N, void* stream) {
+  if (B < 0 || H < 0 || N < 0) return fail(sma::kErrArg, "pack_mask: negative dimension");
+  if (B == 0 || H == 0 || N == 0) return sma::kOk;
+  if (mask == nullptr || packed == nullptr) return fail(sma::kErrArg, "pack_mask: null pointer");
+  const char* msg = nullptr;
+  int rc = sma::launch_pack_mask(static_cast<const uint8_t*>(mask), static_cast<uint32_t*>(packed), B * H * N,
+                                 N, static_cast<cudaStream_t>(stream), &msg);
+  return rc == sma::kOk ? rc : fail(rc, msg);
+}
+
+int sma_attn_fwd(int dtype, const void* q, const void* k, const void* v, const void* mask_packed, void* out,
+                 float* lse, int64_t B, int64_t H, int64_t N, int64_t D, float scale, void* stream) {
+  if (dtype != SMA_DTYPE_FP16 && dtype != SMA_DTYPE_BF16)
+    return fail(sma::kErrDtype, "attention: unsupported dtype, need fp16 or bf16");
+  if (B < 0 || H < 0 || N < 0 || D <= 0) return fail(sma::kErrArg, "attention: bad dimension");
+  if (D != 64 && D != 128) return fail(sma::kErrUnsupportedD, "attention: head dim must be 64 or 128");
+  if (N > SMA_MAX_SEQ_LEN)
+    return fail(sma::kErrUnsupportedN, "attention: sequence length above the supported maximum (8192)");
+  if (B == 0 || H == 0 || N == 0) return sma::kOk;
+  if (!q || !k || !v || !mask_packed || !out) return fail(sma::kErrArg, "attention: null pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))
+    return fail(sma::kErrArg, "attention: q/k/v/out must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(mask_packed) & 3u) != 0 || (lse && (reinterpret_cast<uintptr_t>(lse) & 3u)))
+    return fail(sma::kErrArg, "attention: mask_packed/lse must be 4-byte aligned");
+  uint32_t* err = nullptr;
+  int rc = error_word(&err);
+  if (rc != sma::kOk) return rc;
+  sma::AttnParams p{};
+  p.dtype = dtype;
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.mask = static_cast<const uint32_t*>(mask_packed);
+  p.out = out;
+  p.lse = lse;
+  p.B = B;
+  p.H = H;
+  p.N = N;
+  p.D = D;
+  p.scale = scale;
+  p.err_word = err;
+  p.timeout_ns = g_timeout_ns;
+  p.stream = static_cast<cudaStream_t>(stream);
+  const char* msg = nullptr;
+  rc = sma::launch_attn_fwd(p, &msg);
+  return rc == sma::kOk ? rc : fail(rc, msg);
+}
+
+int sma_device_status(void* stream, int clear) {
+  uint32_t* err = nullptr;
+  int rc = error_word(&err);
+  if (rc != sma::kOk) return rc;
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail_cuda(e, "cudaStreamSynchronize");
+  uint32_t v = 0;
+  e = cudaMemcpy(&v, err, sizeof(v), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return fail_cuda(e, "read device error word");
+  if (clear) {
+    e = cudaMemset(err, 0, sizeof(uint32_t));
+    if (e != cudaSuccess) return fail_cuda(e, "clear device error word");
+    e = cudaDeviceSynchronize();
+    if (e != cudaSuccess) return fail_cuda(e, "clear device error word");
+  }
+  if (v & sma::kDevErrTimeout) return fail(sma::kErrTimeout, "a device-side wait timed out");
+  return sma::kOk;
+}
+
+int sma_set_wait_timeout_ns(uint64_t ns) {
+  if (ns == 0) return fail(sma::kErrArg, "timeout must be positive");
+  g_timeout_ns = ns;
+  return sma::kOk;
+}
+
+int sma_debug_wait_probe(uint64_t timeout_ns, void* stream) {
+  uint32_t* err = nullptr;
+  int rc = error_word(&err);
+  if (rc != sma::kOk) return rc;
+  rc = sma::launch_wait_probe(err, timeout_ns, static_cast<cudaStream_t>(stream));
+  return rc == sma::kOk ? rc : fail(rc, "wait probe launch failed");
+}
+
+const char* sma_last_error(void) { return g_last_error.c_str(); }
+
+int sma_abi_version(void) { return SMA_ABI_VERSION; }
+
+}  // extern "C"

@@ -1,0 +1,53 @@
+// Internal launcher interface shared by the kernel translation units and the
+// C-ABI layer (sma_capi.cu).  Nothing here is exported from the library.
+#pragma once
+
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace sma {
+
+// Status codes (mirrored by the public SMA_* values in include/sma_capi.h).
+enum : int {
+  kOk = 0,
+  kErrArg = 1,
+  kErrDtype = 2,
+  kErrUnsupportedD = 3,
+  kErrLaunch = 4,
+  kErrTimeout = 5,
+  kErrUnsupportedN = 6,
+  kErrCuda = 7,
+};
+
+struct AttnParams {
+  int dtype;                  // 0 = fp16, 1 = bf16
+  const void* q;              // [B, H, N, D] contiguous
+  const void* k;
+  const void* v;
+  const uint32_t* mask;       // [B, H, N, ceil(N/32)] packed bits, LSB = lowest column
+  void* out;                  // [B, H, N, D] contiguous
+  float* lse;                 // [B, H, N] or nullptr
+  int64_t B, H, N, D;
+  float scale;
+  uint32_t* err_word;         // device word the kernel ORs error bits into
+  uint64_t timeout_ns;        // bound on every device-side wait
+  cudaStream_t stream;
+};
+
+// Largest sequence length the fused kernel stages a full mask row-block for.
+constexpr int64_t kMaxSeqLen = 8192;
+
+int launch_pack_mask(const uint8_t* mask, uint32_t* packed, int64_t rows, int64_t n,
+                     cudaStream_t stream, const char** msg);
+
+int launch_attn_fwd(const AttnParams& p, const char** msg);
+
+// Launches one CTA that waits on an mbarrier nothing ever arrives on, using
+// the same bounded-wait helper as the attention kernel; it must give up after
+// `timeout_ns` and set bit 1 of *err_word.
+int launch_wait_probe(uint32_t* err_word, uint64_t timeout_ns, cudaStream_t stream);
+
+// Device error bits.
+constexpr uint32_t kDevErrTimeout = 1u;
+
+}  // namespace sma

@@ -1,0 +1,10 @@
+"""B200-native sparse-mask attention (drop-in for the reference's ``python`` package)."""
+
+from .sparse_attention import (
+    SparseAttentionFunction,
+    pack_mask,
+    sparse_attention,
+    sparse_attention_func,
+)
+
+__all__ = ["sparse_attention", "sparse_attention_func", "pack_mask", "SparseAttentionFunction"]

@@ -1,0 +1,98 @@
+"""Sparse-mask attention: the reference's Python API on the B200 kernels.
+
+Mirrors python/sparse_attention.py of yulangz/sparse-mask-attention-auto-research:
+
+    sparse_attention(q, k, v, mask)       -> out        (:122-156)
+    sparse_attention_func(q, k, v, mask)  -> out        (:159-181, no autograd)
+    pack_mask(mask)                       -> int32 bits (:189-206)
+    SparseAttentionFunction                              (:52-114)
+
+Inputs are q, k, v [B, H, N, D] (fp16 / bf16, or fp32 which is computed in
+bf16 and cast back, as the reference does) and a bool mask [B, H, N, N]
+(True = attend).  The softmax scale is 1/sqrt(D).  Rows whose mask is all
+False produce 0.
+
+Differences from the reference, all deliberate:
+  * CUDA tensors only.  The reference silently falls back to an FP32 PyTorch
+    computation for CPU tensors or a missing extension; here both raise
+    RuntimeError (the FP32 reference lives in the test oracle, not here).
+  * ``sparse_attention_func`` works (the reference passes lse=None to a
+    binding that rejects it).
+  * ``SparseAttentionFunction.backward`` raises: the reference's CUDA
+    backward is an unbound stub (AttributeError when called).
+"""
+
+import math
+
+import torch
+from torch.autograd import Function
+
+from . import sparse_attn_cuda
+
+
+class SparseAttentionFunction(Function):
+    """Autograd wrapper; forward writes O and the FP32 log-sum-exp like the
+    reference (python/sparse_attention.py:52-80, is_training=True)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, mask_packed, mask_bool, scale, seq_len):
+        B, H, N, D = q.shape
+        out = torch.empty_like(q)
+        lse = torch.empty(B, H, N, device=q.device, dtype=torch.float32)
+        sparse_attn_cuda.forward(q, k, v, mask_packed, out, lse, scale, True)
+        ctx.save_for_backward(q, k, v, out, lse, mask_packed, mask_bool)
+        ctx.scale = scale
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        raise RuntimeError(
+            "sparse_attention backward is not implemented by the B200 kernels "
+            "(the reference's CUDA backward is an unbound stub as well)"
+        )
+
+
+def _check_inputs(q, k, v, mask):
+    assert q.shape == k.shape == v.shape, "q/k/v must have the same shape"
+    assert q.device == k.device == v.device == mask.device, "all tensors must be on the same device"
+    assert mask.dtype == torch.bool, "mask must be a bool tensor"
+    if not q.is_cuda:
+        raise RuntimeError("sparse_attention requires CUDA tensors (no CPU fallback)")
+
+
+def sparse_attention(q, k, v, mask):
+    """Masked-softmax attention; returns [B, H, N, D] in the input dtype."""
+    _check_inputs(q, k, v, mask)
+    B, H, N, D = q.shape
+    scale = 1.0 / math.sqrt(D)
+    orig_dtype = q.dtype
+    if orig_dtype == torch.float32:
+        q, k, v = q.bfloat16(), k.bfloat16(), v.bfloat16()
+    mask_packed = pack_mask(mask)
+    out = SparseAttentionFunction.apply(q, k, v, mask_packed, mask, scale, N)
+    if orig_dtype == torch.float32:
+        out = out.float()
+    return out
+
+
+def sparse_attention_func(q, k, v, mask):
+    """Inference variant without autograd and without the LSE output."""
+    _check_inputs(q, k, v, mask)
+    B, H, N, D = q.shape
+    scale = 1.0 / math.sqrt(D)
+    orig_dtype = q.dtype
+    if orig_dtype == torch.float32:
+        q, k, v = q.bfloat16(), k.bfloat16(), v.bfloat16()
+    with torch.no_grad():
+        mask_packed = pack_mask(mask)
+        out = torch.empty_like(q)
+        sparse_attn_cuda.forward(q, k, v, mask_packed, out, None, scale, False)
+    if orig_dtype == torch.float32:
+        out = out.float()
+    return out
+
+
+def pack_mask(mask: torch.Tensor) -> torch.Tensor:
+    """bool [B, H, N, N] -> int32 [B, H, N, ceil(N/32)], bit b of word w =
+    mask[..., 32*w + b]; bits past N are 0.  Bit-identical to the reference."""
+    return sparse_attn_cuda.pack_mask(mask)

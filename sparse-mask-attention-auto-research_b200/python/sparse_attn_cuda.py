@@ -1,0 +1,120 @@
+"""Drop-in for the reference's compiled extension module ``sparse_attn_cuda``.
+
+Same two functions with the same signatures as the pybind module
+(csrc/binding.cpp:68-71), implemented over the C ABI of libsma.so:
+
+    forward(q, k, v, mask_packed, out, lse, scale, is_training) -> None
+    pack_mask(mask) -> torch.int32 tensor [B, H, N, ceil(N/32)]
+
+Error behaviour follows the reference's TORCH_CHECKs (RuntimeError for
+non-CUDA or non-4-D inputs and for dtypes other than fp16/bf16) and adds
+the checks the reference leaves out (matching shapes, contiguity, packed
+mask geometry), since the raw kernels would otherwise read out of bounds.
+``lse`` may be None when ``is_training`` is False (the reference's
+``sparse_attention_func`` passes None there and fails to bind it).
+
+Work is enqueued on the current CUDA stream of the tensors' device,
+asynchronously, like the reference.
+"""
+
+import torch
+
+from . import _lib
+
+_DTYPES = {torch.float16: _lib.SMA_DTYPE_FP16, torch.bfloat16: _lib.SMA_DTYPE_BF16}
+
+
+def _stream_ptr(device):
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _require(cond, msg):
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def forward(q, k, v, mask_packed, out, lse, scale, is_training):
+    """Sparse attention forward (reference csrc/binding.cpp:9-47)."""
+    _require(q.is_cuda, "q must be CUDA tensor")
+    _require(q.dim() == 4, "q must be 4D")
+    _require(q.dtype in _DTYPES, "Unsupported dtype, need BF16 or FP16")
+    B, H, N, D = q.shape
+    for name, t in (("k", k), ("v", v), ("out", out)):
+        _require(t.device == q.device, f"{name} must be on the same device as q")
+        _require(t.shape == q.shape, f"{name} must have the shape of q {tuple(q.shape)}")
+        _require(t.dtype == q.dtype, f"{name} must have the dtype of q")
+        _require(t.is_contiguous(), f"{name} must be contiguous")
+    _require(q.is_contiguous(), "q must be contiguous")
+    n_words = (N + 31) // 32
+    _require(mask_packed.device == q.device, "mask_packed must be on the same device as q")
+    _require(mask_packed.dtype in (torch.int32, torch.uint32), "mask_packed must be int32/uint32")
+    _require(
+        tuple(mask_packed.shape) == (B, H, N, n_words),
+        f"mask_packed must have shape {(B, H, N, n_words)}, got {tuple(mask_packed.shape)}",
+    )
+    _require(mask_packed.is_contiguous(), "mask_packed must be contiguous")
+    lse_ptr = None
+    if is_training:
+        _require(lse is not None, "lse is required when is_training is true")
+        _require(lse.device == q.device, "lse must be on the same device as q")
+        _require(lse.dtype == torch.float32, "lse must be float32")
+        _require(tuple(lse.shape) == (B, H, N), f"lse must have shape {(B, H, N)}")
+        _require(lse.is_contiguous(), "lse must be contiguous")
+        lse_ptr = lse.data_ptr()
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        _lib.check(
+            lib.sma_attn_fwd(
+                _DTYPES[q.dtype],
+                q.data_ptr(),
+                k.data_ptr(),
+                v.data_ptr(),
+                mask_packed.data_ptr(),
+                out.data_ptr(),
+                lse_ptr,
+                B,
+                H,
+                N,
+                D,
+                float(scale),
+                _stream_ptr(q.device),
+            )
+        )
+
+
+def pack_mask(mask):
+    """bool [B, H, N, N] -> int32 [B, H, N, ceil(N/32)] (reference csrc/binding.cpp:49-66)."""
+    _require(mask.is_cuda, "mask must be CUDA tensor")
+    _require(mask.dim() == 4, "mask must be 4D [B, H, N, N]")
+    _require(mask.dtype == torch.bool, "mask must be a bool tensor")
+    B, H, N, N2 = mask.shape
+    _require(N == N2, f"mask must be square in its last two dims, got {tuple(mask.shape)}")
+    mask = mask.contiguous()
+    packed = torch.empty((B, H, N, (N + 31) // 32), dtype=torch.int32, device=mask.device)
+    lib = _lib.load()
+    with torch.cuda.device(mask.device):
+        _lib.check(lib.sma_pack_mask(mask.data_ptr(), packed.data_ptr(), B, H, N, _stream_ptr(mask.device)))
+    return packed
+
+
+def device_status(clear=True, device=None):
+    """Synchronise and raise SmaError if a device-side wait of this library
+    timed out on ``device`` (default: current device) since the last clear."""
+    lib = _lib.load()
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        _lib.check(lib.sma_device_status(_stream_ptr(dev), 1 if clear else 0))
+
+
+def set_wait_timeout_ns(ns):
+    """Upper bound (ns) of every device-side wait in later launches."""
+    _lib.check(_lib.load().sma_set_wait_timeout_ns(int(ns)))
+
+
+def debug_wait_probe(timeout_ns, device=None):
+    """Launch the bounded-wait probe (a wait nothing satisfies); see
+    include/sma_capi.h.  Follow with device_status() to observe the timeout."""
+    lib = _lib.load()
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    with torch.cuda.device(dev):
+        _lib.check(lib.sma_debug_wait_probe(int(timeout_ns), _stream_ptr(dev)))

@@ -1,0 +1,90 @@
+"""The C-ABI library loads without a GPU, exports every symbol its header
+declares, and rejects bad arguments before touching the device.  CPU only:
+no call here launches work."""
+
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import REPO
+
+import python._lib as L  # noqa: E402
+
+HEADER = os.path.join(REPO, "include", "sma_capi.h")
+
+
+def header_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(sma_[a-z0-9_]+)\s*\(", text)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not os.path.exists(L.LIB_PATH):
+        pytest.fail("libsma.so is not built (run __graft_entry__.build())")
+    return L.load()
+
+
+def test_header_declares_the_boundary():
+    fns = header_functions()
+    for name in ("sma_pack_mask", "sma_attn_fwd", "sma_last_error", "sma_device_status"):
+        assert name in fns
+
+
+def test_every_declared_symbol_is_exported(lib):
+    for name in header_functions():
+        assert hasattr(lib, name), name
+    assert set(header_functions()) == set(L.SIGNATURES), "ctypes signature table out of sync with the header"
+
+
+def test_abi_version(lib):
+    assert lib.sma_abi_version() == 1
+
+
+def _attn(lib, dtype=0, q=16, k=16, v=16, m=16, o=16, lse=None, B=1, H=1, N=64, D=64):
+    return lib.sma_attn_fwd(dtype, q, k, v, m, o, lse, B, H, N, D, 0.125, None)
+
+
+def test_attn_rejects_bad_dtype(lib):
+    assert _attn(lib, dtype=7) == L.SMA_ERR_DTYPE
+    assert b"dtype" in lib.sma_last_error()
+
+
+def test_attn_rejects_head_dim(lib):
+    for d in (32, 96, 256):
+        assert _attn(lib, D=d) == L.SMA_ERR_UNSUPPORTED_D
+
+
+def test_attn_rejects_long_sequence(lib):
+    assert _attn(lib, N=L.SMA_MAX_SEQ_LEN + 1) == L.SMA_ERR_UNSUPPORTED_N
+
+
+def test_attn_rejects_bad_args(lib):
+    assert _attn(lib, B=-1) == L.SMA_ERR_ARG
+    assert _attn(lib, q=None) == L.SMA_ERR_ARG
+    assert _attn(lib, q=8) == L.SMA_ERR_ARG  # not 16-byte aligned
+    assert b"aligned" in lib.sma_last_error()
+
+
+def test_empty_problems_are_noops(lib):
+    assert _attn(lib, B=0) == L.SMA_OK
+    assert lib.sma_pack_mask(None, None, 0, 4, 64, None) == L.SMA_OK
+
+
+def test_pack_rejects_bad_args(lib):
+    assert lib.sma_pack_mask(None, None, 1, 1, 64, None) == L.SMA_ERR_ARG
+    assert lib.sma_pack_mask(16, 16, -1, 1, 64, None) == L.SMA_ERR_ARG
+
+
+def test_timeout_setter(lib):
+    assert lib.sma_set_wait_timeout_ns(0) == L.SMA_ERR_ARG
+    assert lib.sma_set_wait_timeout_ns(2_000_000_000) == L.SMA_OK
+
+
+def test_check_raises_with_message(lib):
+    _attn(lib, dtype=9)
+    with pytest.raises(L.SmaError, match="dtype"):
+        L.check(L.SMA_ERR_DTYPE)

@@ -1,0 +1,77 @@
+"""The oracle pinned against the reference's own outputs (tests/golden/, made
+by running the reference's CPU code).  CPU only."""
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import FLT_MAX, golden_ids, golden_path, golden_paths, load_golden
+from oracle import oracle
+
+
+@pytest.mark.parametrize("path", golden_paths("pack") + golden_paths("attn"), ids=golden_ids("pack") + golden_ids("attn"))
+def test_pack_bit_exact_vs_reference(path):
+    case = load_golden(path)
+    got = oracle.pack_mask(case["mask"].numpy())
+    want = case["packed"].numpy()
+    assert got.dtype == np.int32
+    assert got.shape == want.shape
+    assert np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("path", golden_paths("pack"), ids=golden_ids("pack"))
+def test_unpack_roundtrip(path):
+    case = load_golden(path)
+    n = case["mask"].shape[-1]
+    assert np.array_equal(oracle.unpack_mask(case["packed"].numpy(), n), case["mask"].numpy())
+
+
+def test_bit31_is_sign_bit():
+    case = load_golden(golden_path("pack_bit31"))
+    p = oracle.pack_mask(case["mask"].numpy())
+    assert (p == np.int32(-2147483648)).all()
+
+
+@pytest.mark.parametrize("path", golden_paths("attn"), ids=golden_ids("attn"))
+def test_attention_vs_reference(path):
+    case = load_golden(path)
+    scale = case["meta"]["scale"]
+    q, k, v, m = (case[x].float().numpy() for x in ("q", "k", "v", "mask"))
+    out = oracle.attention(q, k, v, m, scale)
+    np.testing.assert_allclose(out, case["out"].numpy(), atol=2e-5, rtol=1e-4)
+    lse = oracle.lse(q, k, m, scale)
+    want = case["lse"].numpy().copy()
+    want[np.isneginf(want)] = -FLT_MAX  # reference CUDA convention for empty rows
+    np.testing.assert_allclose(lse, want, atol=2e-5, rtol=1e-5)
+
+
+def test_parallel_matches_serial():
+    case = load_golden(golden_path("attn_c2_mini"))
+    scale = case["meta"]["scale"]
+    q, k, v, m = (case[x].float().numpy() for x in ("q", "k", "v", "mask"))
+    out, lse = oracle.attention_parallel(q, k, v, m, scale, threads=3, with_lse=True, chunk=1)
+    assert np.array_equal(out, oracle.attention(q, k, v, m, scale))
+    assert np.array_equal(lse, oracle.lse(q, k, m, scale))
+    assert np.array_equal(oracle.pack_mask_parallel(m.astype(bool), threads=3, chunk=1), oracle.pack_mask(m))
+
+
+def test_empty_rows_are_zero():
+    rng = np.random.default_rng(0)
+    q, k, v = (rng.standard_normal((1, 1, 16, 64)).astype(np.float32) for _ in range(3))
+    m = rng.random((1, 1, 16, 16)) < 0.5
+    m[0, 0, 3] = False
+    out = oracle.attention(q, k, v, m, 0.125)
+    assert np.all(out[0, 0, 3] == 0)
+    assert oracle.lse(q, k, m, 0.125)[0, 0, 3] == -FLT_MAX
+
+
+def test_planted_error_is_caught():
+    """A mistake planted in the oracle's inputs must break agreement with the
+    reference fixture (guards against a vacuous comparison)."""
+    case = load_golden(golden_path("attn_c1_mini"))
+    m = case["mask"].numpy().copy()
+    m[0, 0, 10, np.argmax(m[0, 0, 10])] = False  # drop one kept key
+    out = oracle.attention(*(case[x].float().numpy() for x in ("q", "k", "v")), m, case["meta"]["scale"])
+    assert np.abs(out - case["out"].numpy()).max() > 1e-3
+    packed = oracle.pack_mask(m)
+    assert not np.array_equal(packed, case["packed"].numpy())
