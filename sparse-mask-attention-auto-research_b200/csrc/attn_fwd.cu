@@ -22,16 +22,19 @@
 // Per live key tile i the pipeline is
 //   TMA K_i,V_i -> MMA S = Q K_i^T (TMEM) -> softmax: S -> P (fp16/bf16 in TMEM)
 //   -> MMA O += P V_i (A operand straight from TMEM)
-// with a 2-stage K/V ring, and with QK^T of tile i+1 running on the tensor
-// core while the softmax warps exponentiate tile i.
+// with a K/V stage ring.  S is released as soon as the softmax warps have
+// copied it to registers (and is double-buffered when TMEM allows), so QK^T
+// of tile i+1 runs on the tensor core while tile i is exponentiated, and
+// PV of tile i-1 runs while tile i's row maxima are reduced.
 //
 // Softmax: base-2 online softmax in FP32 registers.  The running maximum is
 // only raised when a tile's maximum exceeds it by more than 8 (log2 units),
 // so rescaling the O accumulator in TMEM is rare; values of P stay <= 2^8.
 //
-// TMEM columns (256 allocated, two CTAs per SM):  S [0,BN)  P [BN, 1.5 BN)
-// O [256-D, 256).
+// TMEM columns (256 allocated, two CTAs per SM):
+//   S buffers [0, kSBuf*BN)   P [kSBuf*BN, +BN/2)   O [256-D, 256)
 #include <cfloat>
+#include <cstdlib>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
@@ -44,9 +47,9 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kThreads = 192;
-constexpr int kStages = 2;
 constexpr int kTmemCols = 256;
 constexpr int kMaxTiles = 128;  // kMaxSeqLen / 64
+constexpr int kMaxStages = 4;
 constexpr int kMaxDevices = 64;
 constexpr size_t kMinSmemPerCta = 80 * 1024;  // > 228 KiB / 3
 constexpr float kRescaleThreshold = 8.0f;
@@ -57,14 +60,19 @@ template <int D, int BN>
 struct Cfg {
   static_assert(D == 64 || D == 128, "head dim");
   static_assert(BN == 64 || BN == 128, "key tile");
-  static_assert(BN + BN / 2 <= kTmemCols - D, "TMEM budget");
   static constexpr int kDChunks = D / 64;          // 128-byte swizzle chunks per row
   static constexpr int kQBytes = kBM * D * 2;
   static constexpr int kKBytes = BN * D * 2;
   static constexpr int kStageBytes = 2 * kKBytes;  // K + V
+  // Two S buffers when they fit next to P and O in half of TMEM.
+  static constexpr int kSBuf = (2 * BN + BN / 2 + D <= kTmemCols) ? 2 : 1;
   static constexpr int kSCol = 0;
-  static constexpr int kPCol = BN;
+  static constexpr int kPCol = kSBuf * BN;
   static constexpr int kOCol = kTmemCols - D;
+  static_assert(kPCol + BN / 2 <= kOCol, "TMEM budget");
+  // K/V ring depth: as deep as 64 KiB of shared memory allows.
+  static constexpr int kStages = (65536 / kStageBytes) < kMaxStages ? (65536 / kStageBytes) : kMaxStages;
+  static_assert(kStages >= 2, "stages");
   static constexpr int kWordsPerTile = BN / 32;
 };
 
@@ -72,10 +80,10 @@ struct SharedCtl {
   uint64_t q_full;
   uint64_t mask_full;
   uint64_t sched;
-  uint64_t kv_full[kStages];
-  uint64_t kv_empty[kStages];
-  uint64_t s_full;
-  uint64_t s_free;
+  uint64_t kv_full[kMaxStages];
+  uint64_t kv_empty[kMaxStages];
+  uint64_t s_full[2];
+  uint64_t s_free[2];
   uint64_t p_full;
   uint64_t pv_done;
   uint64_t drain;
@@ -89,6 +97,12 @@ __device__ __forceinline__ float ex2f(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 template <bool BF16>
@@ -118,16 +132,17 @@ __global__ void __launch_bounds__(kThreads, 2)
                     const uint32_t* __restrict__ mask, float* __restrict__ lse, int N, int BH, int W,
                     int KT, float scale_log2, uint32_t* err_word, uint64_t timeout_ns) {
   using C = Cfg<D, BN>;
+  constexpr int S = C::kStages;
   __shared__ SharedCtl ctl;
   extern __shared__ uint8_t dyn_smem[];
 
-  // 1024-byte aligned carve-up: Q | stage0 (K,V) | stage1 (K,V) | mask rows
+  // 1024-byte aligned carve-up: Q | S x (K, V) | mask rows
   const uint32_t raw_base = smem_u32(dyn_smem);
   const uint32_t base = (raw_base + 1023u) & ~1023u;
   uint8_t* base_ptr = dyn_smem + (base - raw_base);
   const uint32_t sQ = base;
   const uint32_t sStage = sQ + C::kQBytes;
-  uint32_t* smask = reinterpret_cast<uint32_t*>(base_ptr + C::kQBytes + kStages * C::kStageBytes);
+  uint32_t* smask = reinterpret_cast<uint32_t*>(base_ptr + C::kQBytes + S * C::kStageBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -145,12 +160,14 @@ __global__ void __launch_bounds__(kThreads, 2)
     mbar_init(smem_u32(&ctl.q_full), 1);
     mbar_init(smem_u32(&ctl.mask_full), 1);
     mbar_init(smem_u32(&ctl.sched), 1);
-    for (int s = 0; s < kStages; ++s) {
+    for (int s = 0; s < S; ++s) {
       mbar_init(smem_u32(&ctl.kv_full[s]), 1);
       mbar_init(smem_u32(&ctl.kv_empty[s]), 1);
     }
-    mbar_init(smem_u32(&ctl.s_full), 1);
-    mbar_init(smem_u32(&ctl.s_free), 4);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&ctl.s_full[b]), 1);
+      mbar_init(smem_u32(&ctl.s_free[b]), 4);
+    }
     mbar_init(smem_u32(&ctl.p_full), 4);
     mbar_init(smem_u32(&ctl.pv_done), 1);
     mbar_init(smem_u32(&ctl.drain), 1);
@@ -233,10 +250,9 @@ __global__ void __launch_bounds__(kThreads, 2)
       // K/V loads for live tiles through the stage ring.
       int issued = 0;
       for (uint32_t i = 0; i < n_live; ++i) {
-        const int stage = i % kStages;
-        if (i >= kStages) {
-          if (!mbar_wait_bounded(smem_u32(&ctl.kv_empty[stage]), ((i / kStages) - 1) & 1, abort_flag,
-                                 timeout_ns)) {
+        const int stage = i % S;
+        if (i >= S) {
+          if (!mbar_wait_bounded(smem_u32(&ctl.kv_empty[stage]), ((i / S) - 1) & 1, abort_flag, timeout_ns)) {
             record_abort(&ctl, err_word);
             break;
           }
@@ -257,8 +273,8 @@ __global__ void __launch_bounds__(kThreads, 2)
         // (these waits ignore the abort flag; copies need no other role).
         uint32_t zero = 0;
         mbar_wait_bounded(smem_u32(&ctl.q_full), 0, &zero, timeout_ns);
-        for (int j = (issued > kStages ? issued - kStages : 0); j < issued; ++j)
-          mbar_wait_bounded(smem_u32(&ctl.kv_full[j % kStages]), (j / kStages) & 1, &zero, timeout_ns);
+        for (int j = (issued > S ? issued - S : 0); j < issued; ++j)
+          mbar_wait_bounded(smem_u32(&ctl.kv_full[j % S]), (j / S) & 1, &zero, timeout_ns);
       }
     }
   } else if (warp == 5) {
@@ -270,27 +286,31 @@ __global__ void __launch_bounds__(kThreads, 2)
       const uint32_t n = ok ? ctl.n_live : 0u;
       if (ok && n > 0) ok = mbar_wait_bounded(smem_u32(&ctl.q_full), 0, abort_flag, timeout_ns);
       auto issue_pv = [&](uint32_t j) {
-        const int stage = j % kStages;
+        const int stage = j % S;
         const uint32_t sV = sStage + stage * C::kStageBytes + C::kKBytes;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           const uint64_t bdesc = smem_desc_sw128(sV + kk * 2048, BN * 128, 1024);
           mma_ts(tmem + C::kOCol, tmem + C::kPCol + kk * 8, bdesc, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
         }
-        // The producer only waits for a stage it will refill; the last
-        // kStages tiles release nothing, so no asynchronous arrive can
-        // outlive the CTA (pv_done of the last tile is awaited by the epilogue).
-        if (j + kStages < n) mma_commit(smem_u32(&ctl.kv_empty[stage]));
+        // The producer only waits for a stage it will refill; the last S
+        // tiles release nothing, so no asynchronous arrive can outlive the
+        // CTA (pv_done of the last tile is awaited by the epilogue).
+        if (j + S < n) mma_commit(smem_u32(&ctl.kv_empty[stage]));
         mma_commit(smem_u32(&ctl.pv_done));
       };
       uint32_t i = 0;
       for (; ok && i < n; ++i) {
-        const int stage = i % kStages;
-        if (!mbar_wait_bounded(smem_u32(&ctl.kv_full[stage]), (i / kStages) & 1, abort_flag, timeout_ns)) {
+        const int stage = i % S;
+        const int sb = i % C::kSBuf;
+        if (!mbar_wait_bounded(smem_u32(&ctl.kv_full[stage]), (i / S) & 1, abort_flag, timeout_ns)) {
           ok = false;
           break;
         }
-        if (i > 0 && !mbar_wait_bounded(smem_u32(&ctl.s_free), (i - 1) & 1, abort_flag, timeout_ns)) {
+        // S buffer sb was last read by the softmax of tile i - kSBuf.
+        if (i >= static_cast<uint32_t>(C::kSBuf) &&
+            !mbar_wait_bounded(smem_u32(&ctl.s_free[sb]), ((i - C::kSBuf) / C::kSBuf) & 1, abort_flag,
+                               timeout_ns)) {
           ok = false;
           break;
         }
@@ -300,10 +320,10 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t koff = (kk >> 2) * (BN * 128) + (kk & 3) * 32;
           const uint32_t qoff = (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
-          mma_ss(tmem + C::kSCol, smem_desc_sw128(sQ + qoff, 16, 1024), smem_desc_sw128(sK + koff, 16, 1024),
-                 idesc_qk, kk > 0 ? 1u : 0u);
+          mma_ss(tmem + C::kSCol + sb * BN, smem_desc_sw128(sQ + qoff, 16, 1024),
+                 smem_desc_sw128(sK + koff, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
         }
-        mma_commit(smem_u32(&ctl.s_full));
+        mma_commit(smem_u32(&ctl.s_full[sb]));
         if (i > 0) {
           if (!mbar_wait_bounded(smem_u32(&ctl.p_full), (i - 1) & 1, abort_flag, timeout_ns)) {
             ok = false;
@@ -334,13 +354,15 @@ __global__ void __launch_bounds__(kThreads, 2)
     const int r = threadIdx.x;  // query row within the tile == TMEM lane
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     float m_run = -INFINITY;  // running max of scale*log2(e)*s (may lag the true max by <= 8)
-    float l_run = 0.f;
+    float l_run = 0.f;        // sum of 2^(x - m_run), FP32 weights (for the LSE)
+    float l_out = 0.f;        // the same over the weights as rounded for the PV MMA (normalises O)
     bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&ctl.sched), 0, abort_flag, timeout_ns));
     const uint32_t n = ok ? ctl.n_live : 0u;
     const uint32_t* mrow = smask + r * W;
 
     for (uint32_t i = 0; ok && i < n; ++i) {
       const int kt = ctl.live[i];
+      const int sb = i % C::kSBuf;
       uint32_t mw[C::kWordsPerTile];
 #pragma unroll
       for (int w = 0; w < C::kWordsPerTile; ++w) {
@@ -350,32 +372,37 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (valid < 32) v = (valid <= 0) ? 0u : (v & ((1u << valid) - 1u));
         mw[w] = v;
       }
-      ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&ctl.s_full), i & 1, abort_flag, timeout_ns));
+      ok = __all_sync(0xffffffffu,
+                      mbar_wait_bounded(smem_u32(&ctl.s_full[sb]), (i / C::kSBuf) & 1, abort_flag, timeout_ns));
       if (!ok) break;
       tc_fence_after();
       float s[BN];
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t u[32];
-        tmem_ld32(t_lane + C::kSCol + c * 32, u);
+        tmem_ld32(t_lane + C::kSCol + sb * BN + c * 32, u);
 #pragma unroll
         for (int j = 0; j < 32; ++j) s[c * 32 + j] = __uint_as_float(u[j]);
       }
       tmem_wait_ld();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&ctl.s_free));
+      if (lane == 0) mbar_arrive(smem_u32(&ctl.s_free[sb]));
 
-      float mt = -INFINITY;
+      // Masked row maximum: four independent 3-input max chains.
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
 #pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float v = ((mw[c] >> j) & 1u) ? s[c * 32 + j] : -INFINITY;
-          s[c * 32 + j] = v;
-          mt = fmaxf(mt, v);
+        for (int j = 0; j < 32; j += 2) {
+          const float v0 = (mw[c] & (1u << j)) ? s[c * 32 + j] : -INFINITY;
+          const float v1 = (mw[c] & (2u << j)) ? s[c * 32 + j + 1] : -INFINITY;
+          s[c * 32 + j] = v0;
+          s[c * 32 + j + 1] = v1;
+          mx[(j >> 1) & 3] = max3f(mx[(j >> 1) & 3], v0, v1);
         }
       }
+      const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
       const float x_max = mt * scale_log2;
       float alpha = 1.f;
       bool rescale_o = false;
@@ -385,26 +412,19 @@ __global__ void __launch_bounds__(kThreads, 2)
           rescale_o = true;
         }
         l_run *= alpha;
+        l_out *= alpha;
         m_run = x_max;
       }
       if (i > 0) {
+        // PV of the previous tile still reads P (and accumulates O).
         ok = __all_sync(0xffffffffu,
                         mbar_wait_bounded(smem_u32(&ctl.pv_done), (i - 1) & 1, abort_flag, timeout_ns));
         if (!ok) break;
         tc_fence_after();
-        if (__any_sync(0xffffffffu, rescale_o)) {
-#pragma unroll
-          for (int c = 0; c < D / 32; ++c) {
-            uint32_t u[32];
-            tmem_ld32(t_lane + C::kOCol + c * 32, u);
-            tmem_wait_ld();
-#pragma unroll
-            for (int j = 0; j < 32; ++j) u[j] = __float_as_uint(__uint_as_float(u[j]) * alpha);
-            tmem_st32(t_lane + C::kOCol + c * 32, u);
-          }
-        }
       }
       const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+      float la[4] = {0.f, 0.f, 0.f, 0.f};
+      float lr[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int c = 0; c < BN / 32; ++c) {
         uint32_t pk[16];
@@ -412,10 +432,31 @@ __global__ void __launch_bounds__(kThreads, 2)
         for (int j = 0; j < 16; ++j) {
           const float p0 = ex2f(fmaf(s[c * 32 + 2 * j], scale_log2, -m_use));
           const float p1 = ex2f(fmaf(s[c * 32 + 2 * j + 1], scale_log2, -m_use));
-          l_run += p0 + p1;
           pk[j] = pack2<BF16>(p0, p1);
+          la[j & 3] += p0 + p1;
+          if constexpr (BF16) {
+            // With 8-bit mantissas the rounding of a dominant weight would
+            // show up directly in O: normalise by the weights the MMA uses.
+            lr[j & 3] += __uint_as_float(pk[j] << 16) + __uint_as_float(pk[j] & 0xFFFF0000u);
+          }
         }
         tmem_st16(t_lane + C::kPCol + c * 16, pk);
+      }
+      const float l_tile = (la[0] + la[1]) + (la[2] + la[3]);
+      l_run += l_tile;
+      l_out += BF16 ? (lr[0] + lr[1]) + (lr[2] + lr[3]) : l_tile;
+      if (i > 0 && __any_sync(0xffffffffu, rescale_o)) {
+        // Rare: the running max rose by more than the threshold.  PV of this
+        // tile waits for p_full below, so O can be rescaled in place now.
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t u[32];
+          tmem_ld32(t_lane + C::kOCol + c * 32, u);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) u[j] = __float_as_uint(__uint_as_float(u[j]) * alpha);
+          tmem_st32(t_lane + C::kOCol + c * 32, u);
+        }
       }
       tmem_wait_st();
       tc_fence_before();
@@ -435,7 +476,7 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
     if (!ok && lane == 0) record_abort(&ctl, err_word);
     if (ok) {
-      const float inv = (l_run > 0.f) ? (1.f / l_run) : 0.f;
+      const float inv = (l_out > 0.f) ? (1.f / l_out) : 0.f;
       uint8_t* stage_row = base_ptr + r * 128;  // row r of each 128-row x 64-col chunk
 #pragma unroll
       for (int c = 0; c < D / 32; ++c) {
@@ -451,7 +492,8 @@ __global__ void __launch_bounds__(kThreads, 2)
 #pragma unroll
         for (int j = 0; j < 16; ++j)
           h[j] = pack2<BF16>(__uint_as_float(u[2 * j]) * inv, __uint_as_float(u[2 * j + 1]) * inv);
-        // columns [32c, 32c+32) = 64 bytes = four 16-byte chunks of row r
+        // columns [32c, 32c+32) = 64 bytes = four 16-byte chunks of row r,
+        // stored at the 128-byte-swizzled positions the O tensor map expects
         const int dc = c >> 1;
         uint8_t* chunk_base = stage_row + dc * (kBM * 128);
 #pragma unroll
@@ -537,7 +579,7 @@ int launch_impl(const AttnParams& p, const char** msg) {
   // third resident CTA would block in tcgen05.alloc.  Registers already cap
   // residency at two; the shared-memory floor makes that independent of the
   // register count.
-  size_t smem = 1024 + C::kQBytes + kStages * C::kStageBytes + ((mask_bytes + 15) / 16) * 16;
+  size_t smem = 1024 + C::kQBytes + C::kStages * C::kStageBytes + ((mask_bytes + 15) / 16) * 16;
   if (smem < kMinSmemPerCta) smem = kMinSmemPerCta;
   auto kern = attn_fwd_kernel<D, BN, BF16>;
   // The dynamic shared-memory opt-in is per device; remember the largest
@@ -583,6 +625,17 @@ __global__ void wait_probe_kernel(uint32_t* err_word, uint64_t timeout_ns) {
   }
 }
 
+// Key-tile width for head dim 64: 64 by default (two S buffers in TMEM,
+// half the registers per softmax thread); SMA_ATTN_BN=128 selects the wide
+// tile (one S buffer).  Read once per process.
+int key_tile_d64() {
+  static int bn = [] {
+    const char* e = std::getenv("SMA_ATTN_BN");
+    return (e != nullptr && std::atoi(e) == 128) ? 128 : 64;
+  }();
+  return bn;
+}
+
 }  // namespace
 
 int launch_attn_fwd(const AttnParams& p, const char** msg) {
@@ -591,7 +644,11 @@ int launch_attn_fwd(const AttnParams& p, const char** msg) {
     return kErrUnsupportedN;
   }
   const bool bf = p.dtype == 1;
-  if (p.D == 64) return bf ? launch_impl<64, 128, true>(p, msg) : launch_impl<64, 128, false>(p, msg);
+  if (p.D == 64) {
+    if (key_tile_d64() == 128)
+      return bf ? launch_impl<64, 128, true>(p, msg) : launch_impl<64, 128, false>(p, msg);
+    return bf ? launch_impl<64, 64, true>(p, msg) : launch_impl<64, 64, false>(p, msg);
+  }
   if (p.D == 128) return bf ? launch_impl<128, 64, true>(p, msg) : launch_impl<128, 64, false>(p, msg);
   *msg = "attention: head dim must be 64 or 128";
   return kErrUnsupportedD;
