@@ -32,9 +32,8 @@
 // so rescaling the O accumulator in TMEM is rare; values of P stay <= 2^8.
 //
 // TMEM columns (256 allocated, two CTAs per SM):
-//   S buffers [0, kSBuf*BN)   P [kSBuf*BN, +BN/2)   O [256-D, 256)
+//   S buffers [0, kSBuf*BN)   P buffers [kSBuf*BN, +kPBuf*BN/2)   O [256-D, 256)
 #include <cfloat>
-#include <cstdlib>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
@@ -59,17 +58,20 @@ constexpr float kLog2e = 1.44269504088896340736f;
 template <int D, int BN>
 struct Cfg {
   static_assert(D == 64 || D == 128, "head dim");
-  static_assert(BN == 64 || BN == 128, "key tile");
+  static_assert(BN == 64, "key tile");
   static constexpr int kDChunks = D / 64;          // 128-byte swizzle chunks per row
   static constexpr int kQBytes = kBM * D * 2;
   static constexpr int kKBytes = BN * D * 2;
   static constexpr int kStageBytes = 2 * kKBytes;  // K + V
-  // Two S buffers when they fit next to P and O in half of TMEM.
-  static constexpr int kSBuf = (2 * BN + BN / 2 + D <= kTmemCols) ? 2 : 1;
+  // TMEM buffering within half of TMEM (two CTAs per SM): a second P buffer
+  // first (the softmax then never waits for the previous PV before writing
+  // P), then a second S buffer (QK^T may run two tiles ahead).
+  static constexpr int kPBuf = (BN + 2 * (BN / 2) + D <= kTmemCols) ? 2 : 1;
+  static constexpr int kSBuf = (2 * BN + kPBuf * (BN / 2) + D <= kTmemCols) ? 2 : 1;
   static constexpr int kSCol = 0;
   static constexpr int kPCol = kSBuf * BN;
   static constexpr int kOCol = kTmemCols - D;
-  static_assert(kPCol + BN / 2 <= kOCol, "TMEM budget");
+  static_assert(kPCol + kPBuf * (BN / 2) <= kOCol, "TMEM budget");
   // K/V ring depth: as deep as 64 KiB of shared memory allows.
   static constexpr int kStages = (65536 / kStageBytes) < kMaxStages ? (65536 / kStageBytes) : kMaxStages;
   static_assert(kStages >= 2, "stages");
@@ -84,9 +86,10 @@ struct SharedCtl {
   uint64_t kv_empty[kMaxStages];
   uint64_t s_full[2];
   uint64_t s_free[2];
-  uint64_t p_full;
-  uint64_t pv_done;
+  uint64_t p_full[2];
+  uint64_t pv_done[2];
   uint64_t drain;
+  uint32_t colbits[8];
   uint32_t tmem_base;
   uint32_t n_live;
   uint32_t abort_flag;
@@ -133,16 +136,22 @@ __global__ void __launch_bounds__(kThreads, 2)
                     int KT, float scale_log2, uint32_t* err_word, uint64_t timeout_ns) {
   using C = Cfg<D, BN>;
   constexpr int S = C::kStages;
-  __shared__ SharedCtl ctl;
-  extern __shared__ uint8_t dyn_smem[];
+  extern __shared__ __align__(1024) uint8_t dyn_smem[];
 
-  // 1024-byte aligned carve-up: Q | S x (K, V) | mask rows
-  const uint32_t raw_base = smem_u32(dyn_smem);
-  const uint32_t base = (raw_base + 1023u) & ~1023u;
-  uint8_t* base_ptr = dyn_smem + (base - raw_base);
+  // Carve-up (no static shared memory, so the dynamic window starts on a
+  // 1024-byte boundary as the 128-byte-swizzled tiles require):
+  //   Q | S x (K, V) | mask rows | control block
+  const uint32_t base = smem_u32(dyn_smem);
+  if ((base & 1023u) != 0u) {
+    if (threadIdx.x == 0) atomicOr(err_word, kDevErrLayout);
+    return;
+  }
+  uint8_t* base_ptr = dyn_smem;
   const uint32_t sQ = base;
   const uint32_t sStage = sQ + C::kQBytes;
   uint32_t* smask = reinterpret_cast<uint32_t*>(base_ptr + C::kQBytes + S * C::kStageBytes);
+  SharedCtl& ctl = *reinterpret_cast<SharedCtl*>(base_ptr + C::kQBytes + S * C::kStageBytes +
+                                                 ((static_cast<uint32_t>(kBM) * W * 4u + 15u) & ~15u));
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -167,9 +176,9 @@ __global__ void __launch_bounds__(kThreads, 2)
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&ctl.s_full[b]), 1);
       mbar_init(smem_u32(&ctl.s_free[b]), 4);
+      mbar_init(smem_u32(&ctl.p_full[b]), 4);
+      mbar_init(smem_u32(&ctl.pv_done[b]), 1);
     }
-    mbar_init(smem_u32(&ctl.p_full), 4);
-    mbar_init(smem_u32(&ctl.pv_done), 1);
     mbar_init(smem_u32(&ctl.drain), 1);
     ctl.abort_flag = 0;
     ctl.n_live = 0;
@@ -215,29 +224,35 @@ __global__ void __launch_bounds__(kThreads, 2)
 
     uint32_t n_live = 0;
     if (ok) {
-      // Live key tiles: any of the 128 rows has a set bit in the tile's words.
-      for (int t0 = 0; t0 < KT; t0 += 32) {
-        uint32_t live_bits = 0;
-        const int t_end = min(KT, t0 + 32);
-        for (int t = t0; t < t_end; ++t) {
+      // Column-word liveness: OR of each packed-mask column word over the
+      // 128 rows.  Lanes read consecutive words of a row (no bank conflicts).
+      if (W <= 32 && (32 % W) == 0) {
+        const int c = lane % W, g = lane / W, G = 32 / W;
+        uint32_t acc = 0;
+#pragma unroll 8
+        for (int r = g; r < kBM; r += G) acc |= smask[r * W + c];
+        uint32_t nz = __ballot_sync(0xffffffffu, acc != 0u);
+        for (int sh = W; sh < 32; sh <<= 1) nz |= nz >> sh;  // fold row groups onto columns
+        if (lane == 0) ctl.colbits[0] = (W == 32) ? nz : (nz & ((1u << W) - 1u));
+      } else {
+        for (int c0 = 0; c0 < W; c0 += 32) {
+          const int c = c0 + lane;
           uint32_t acc = 0;
-#pragma unroll
-          for (int rr = 0; rr < 4; ++rr) {
-            const uint32_t* row = smask + (lane + 32 * rr) * W;
-#pragma unroll
-            for (int w = 0; w < C::kWordsPerTile; ++w) {
-              const int cw = t * C::kWordsPerTile + w;
-              if (cw < W) acc |= row[cw];
-            }
+          if (c < W) {
+#pragma unroll 8
+            for (int r = 0; r < kBM; ++r) acc |= smask[r * W + c];
           }
-          if (__ballot_sync(0xffffffffu, acc != 0u) != 0u) live_bits |= 1u << (t - t0);
+          const uint32_t nz = __ballot_sync(0xffffffffu, acc != 0u);
+          if (lane == 0) ctl.colbits[c0 >> 5] = nz;
         }
-        if (lane == 0) {
-          while (live_bits) {
-            const int b = __ffs(live_bits) - 1;
-            live_bits &= live_bits - 1;
-            ctl.live[n_live++] = static_cast<uint16_t>(t0 + b);
-          }
+      }
+      __syncwarp();
+      // A key tile is live when any of its column words is.
+      if (lane == 0) {
+        for (int t = 0; t < KT; ++t) {
+          const int w0 = t * C::kWordsPerTile;
+          const uint32_t bits = (ctl.colbits[w0 >> 5] >> (w0 & 31)) & ((1u << C::kWordsPerTile) - 1u);
+          if (bits) ctl.live[n_live++] = static_cast<uint16_t>(t);
         }
       }
     } else if (lane == 0) {
@@ -287,33 +302,29 @@ __global__ void __launch_bounds__(kThreads, 2)
       if (ok && n > 0) ok = mbar_wait_bounded(smem_u32(&ctl.q_full), 0, abort_flag, timeout_ns);
       auto issue_pv = [&](uint32_t j) {
         const int stage = j % S;
+        const int pb = j % C::kPBuf;
         const uint32_t sV = sStage + stage * C::kStageBytes + C::kKBytes;
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           const uint64_t bdesc = smem_desc_sw128(sV + kk * 2048, BN * 128, 1024);
-          mma_ts(tmem + C::kOCol, tmem + C::kPCol + kk * 8, bdesc, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+          mma_ts(tmem + C::kOCol, tmem + C::kPCol + pb * (BN / 2) + kk * 8, bdesc, idesc_pv,
+                 (j > 0 || kk > 0) ? 1u : 0u);
         }
         // The producer only waits for a stage it will refill; the last S
         // tiles release nothing, so no asynchronous arrive can outlive the
         // CTA (pv_done of the last tile is awaited by the epilogue).
         if (j + S < n) mma_commit(smem_u32(&ctl.kv_empty[stage]));
-        mma_commit(smem_u32(&ctl.pv_done));
+        mma_commit(smem_u32(&ctl.pv_done[pb]));
       };
-      uint32_t i = 0;
-      for (; ok && i < n; ++i) {
-        const int stage = i % S;
-        const int sb = i % C::kSBuf;
-        if (!mbar_wait_bounded(smem_u32(&ctl.kv_full[stage]), (i / S) & 1, abort_flag, timeout_ns)) {
-          ok = false;
-          break;
-        }
-        // S buffer sb was last read by the softmax of tile i - kSBuf.
-        if (i >= static_cast<uint32_t>(C::kSBuf) &&
-            !mbar_wait_bounded(smem_u32(&ctl.s_free[sb]), ((i - C::kSBuf) / C::kSBuf) & 1, abort_flag,
-                               timeout_ns)) {
-          ok = false;
-          break;
-        }
+      // QK^T of tile j into S buffer j % kSBuf, once K_j has landed and the
+      // softmax has copied out the S of tile j - kSBuf.
+      auto issue_qk = [&](uint32_t j) -> bool {
+        const int stage = j % S;
+        const int sb = j % C::kSBuf;
+        if (!mbar_wait_bounded(smem_u32(&ctl.kv_full[stage]), (j / S) & 1, abort_flag, timeout_ns)) return false;
+        if (j >= static_cast<uint32_t>(C::kSBuf) &&
+            !mbar_wait_bounded(smem_u32(&ctl.s_free[sb]), ((j - C::kSBuf) / C::kSBuf) & 1, abort_flag, timeout_ns))
+          return false;
         tc_fence_after();
         const uint32_t sK = sStage + stage * C::kStageBytes;
 #pragma unroll
@@ -324,22 +335,22 @@ __global__ void __launch_bounds__(kThreads, 2)
                  smem_desc_sw128(sK + koff, 16, 1024), idesc_qk, kk > 0 ? 1u : 0u);
         }
         mma_commit(smem_u32(&ctl.s_full[sb]));
-        if (i > 0) {
-          if (!mbar_wait_bounded(smem_u32(&ctl.p_full), (i - 1) & 1, abort_flag, timeout_ns)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          issue_pv(i - 1);
-        }
-      }
-      if (ok && n > 0) {
-        if (mbar_wait_bounded(smem_u32(&ctl.p_full), (n - 1) & 1, abort_flag, timeout_ns)) {
-          tc_fence_after();
-          issue_pv(n - 1);
-        } else {
+        return true;
+      };
+      for (uint32_t j = 0; ok && j < n && j < static_cast<uint32_t>(C::kSBuf); ++j) ok = issue_qk(j);
+      for (uint32_t i = 0; ok && i < n; ++i) {
+        // Tile i + kSBuf's QK^T only needs tile i's S copied out (early in
+        // the softmax of tile i), so it overlaps that softmax.
+        if (i + C::kSBuf < n && !issue_qk(i + C::kSBuf)) {
           ok = false;
+          break;
         }
+        if (!mbar_wait_bounded(smem_u32(&ctl.p_full[i % C::kPBuf]), (i / C::kPBuf) & 1, abort_flag, timeout_ns)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        issue_pv(i);
       }
       if (!ok) {
         record_abort(&ctl, err_word);
@@ -351,6 +362,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     }
   } else {
     // ------------------------------------------------------------ softmax warps 0-3
+    // Software-pipelined over key tiles: while the exponentials of tile i
+    // are computed (MUFU), tile i+1 is copied out of TMEM and its masked row
+    // maximum is reduced (ALU), so both pipes stay busy in every warp.  Each
+    // 32-column chunk of tile i+1 is loaded into the registers the same
+    // chunk of tile i has just been consumed from.
     const int r = threadIdx.x;  // query row within the tile == TMEM lane
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     float m_run = -INFINITY;  // running max of scale*log2(e)*s (may lag the true max by <= 8)
@@ -359,11 +375,11 @@ __global__ void __launch_bounds__(kThreads, 2)
     bool ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&ctl.sched), 0, abort_flag, timeout_ns));
     const uint32_t n = ok ? ctl.n_live : 0u;
     const uint32_t* mrow = smask + r * W;
+    constexpr int kChunks = BN / 32;
 
-    for (uint32_t i = 0; ok && i < n; ++i) {
+    // Mask words of tile i for this row, bits past N cleared.
+    auto mask_words = [&](uint32_t i, uint32_t (&mw)[C::kWordsPerTile]) {
       const int kt = ctl.live[i];
-      const int sb = i % C::kSBuf;
-      uint32_t mw[C::kWordsPerTile];
 #pragma unroll
       for (int w = 0; w < C::kWordsPerTile; ++w) {
         const int cw = kt * C::kWordsPerTile + w;
@@ -372,66 +388,98 @@ __global__ void __launch_bounds__(kThreads, 2)
         if (valid < 32) v = (valid <= 0) ? 0u : (v & ((1u << valid) - 1u));
         mw[w] = v;
       }
-      ok = __all_sync(0xffffffffu,
-                      mbar_wait_bounded(smem_u32(&ctl.s_full[sb]), (i / C::kSBuf) & 1, abort_flag, timeout_ns));
-      if (!ok) break;
-      tc_fence_after();
-      float s[BN];
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t u[32];
-        tmem_ld32(t_lane + C::kSCol + sb * BN + c * 32, u);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) s[c * 32 + j] = __uint_as_float(u[j]);
-      }
+    };
+    // Wait for S of tile i; copy column chunk c (32 columns) to registers.
+    auto wait_s = [&](uint32_t i) -> bool {
+      const bool w = mbar_wait_bounded(smem_u32(&ctl.s_full[i % C::kSBuf]), (i / C::kSBuf) & 1, abort_flag, timeout_ns);
+      const bool all = __all_sync(0xffffffffu, w);
+      if (all) tc_fence_after();
+      return all;
+    };
+    auto load_chunk = [&](uint32_t i, int c, float* dst) {
+      tmem_ld32f(t_lane + C::kSCol + (i % C::kSBuf) * BN + c * 32, dst);
       tmem_wait_ld();
+    };
+    auto release_s = [&](uint32_t i) {
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&ctl.s_free[sb]));
-
-      // Masked row maximum: four independent 3-input max chains.
-      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (lane == 0) mbar_arrive(smem_u32(&ctl.s_free[i % C::kSBuf]));
+    };
+    // Masked values in place (-inf where the bit is clear) and their max.
+    auto mask_max_chunk = [&](float* v, uint32_t word, float (&mx)[4]) {
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
-#pragma unroll
-        for (int j = 0; j < 32; j += 2) {
-          const float v0 = (mw[c] & (1u << j)) ? s[c * 32 + j] : -INFINITY;
-          const float v1 = (mw[c] & (2u << j)) ? s[c * 32 + j + 1] : -INFINITY;
-          s[c * 32 + j] = v0;
-          s[c * 32 + j + 1] = v1;
-          mx[(j >> 1) & 3] = max3f(mx[(j >> 1) & 3], v0, v1);
-        }
+      for (int j = 0; j < 32; j += 2) {
+        const float v0 = (word & (1u << j)) ? v[j] : -INFINITY;
+        const float v1 = (word & (2u << j)) ? v[j + 1] : -INFINITY;
+        v[j] = v0;
+        v[j + 1] = v1;
+        mx[(j >> 1) & 3] = max3f(mx[(j >> 1) & 3], v0, v1);
       }
-      const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3]));
-      const float x_max = mt * scale_log2;
-      float alpha = 1.f;
-      bool rescale_o = false;
+    };
+    // Lazy running-max update from a tile maximum; returns whether the O
+    // accumulator needs rescaling by `alpha` before the next PV.
+    auto update_max = [&](const float (&mx)[4], float& alpha) -> bool {
+      const float x_max = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale_log2;
+      alpha = 1.f;
+      bool rescale = false;
       if (x_max > m_run + kRescaleThreshold) {
         if (m_run != -INFINITY) {
           alpha = ex2f(m_run - x_max);
-          rescale_o = true;
+          rescale = true;
         }
         l_run *= alpha;
         l_out *= alpha;
         m_run = x_max;
       }
-      if (i > 0) {
-        // PV of the previous tile still reads P (and accumulates O).
-        ok = __all_sync(0xffffffffu,
-                        mbar_wait_bounded(smem_u32(&ctl.pv_done), (i - 1) & 1, abort_flag, timeout_ns));
-        if (!ok) break;
+      return rescale;
+    };
+
+    float buf[BN];
+    float alpha_cur = 1.f;
+    bool rescale_cur = false;
+    if (ok && n > 0) {
+      ok = wait_s(0);
+      if (ok) {
+        uint32_t mw[C::kWordsPerTile];
+        mask_words(0, mw);
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int c = 0; c < kChunks; ++c) {
+          load_chunk(0, c, buf + c * 32);
+          mask_max_chunk(buf + c * 32, mw[c], mx);
+        }
+        release_s(0);
+        rescale_cur = update_max(mx, alpha_cur);
+      }
+    }
+
+    // One pipelined step: exponentials of tile i (masked values in `buf`,
+    // running max already settled) interleaved with loading and reducing
+    // tile i+1 into the same registers.
+    auto step = [&](uint32_t i) -> bool {
+      const bool has_next = i + 1 < n;
+      const int pb = i % C::kPBuf;
+      if (has_next && !wait_s(i + 1)) return false;
+      if (i >= static_cast<uint32_t>(C::kPBuf)) {
+        // P buffer pb was last read by the PV of tile i - kPBuf.
+        if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&ctl.pv_done[pb]), ((i - C::kPBuf) / C::kPBuf) & 1,
+                                                        abort_flag, timeout_ns)))
+          return false;
         tc_fence_after();
       }
+      uint32_t mwn[C::kWordsPerTile];
+      if (has_next) mask_words(i + 1, mwn);
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
       const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
       float la[4] = {0.f, 0.f, 0.f, 0.f};
       float lr[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {
+      for (int c = 0; c < kChunks; ++c) {
         uint32_t pk[16];
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
-          const float p0 = ex2f(fmaf(s[c * 32 + 2 * j], scale_log2, -m_use));
-          const float p1 = ex2f(fmaf(s[c * 32 + 2 * j + 1], scale_log2, -m_use));
+          const float p0 = ex2f(fmaf(buf[c * 32 + 2 * j], scale_log2, -m_use));
+          const float p1 = ex2f(fmaf(buf[c * 32 + 2 * j + 1], scale_log2, -m_use));
           pk[j] = pack2<BF16>(p0, p1);
           la[j & 3] += p0 + p1;
           if constexpr (BF16) {
@@ -440,34 +488,51 @@ __global__ void __launch_bounds__(kThreads, 2)
             lr[j & 3] += __uint_as_float(pk[j] << 16) + __uint_as_float(pk[j] & 0xFFFF0000u);
           }
         }
-        tmem_st16(t_lane + C::kPCol + c * 16, pk);
+        tmem_st16(t_lane + C::kPCol + pb * (BN / 2) + c * 16, pk);
+        if (has_next) {
+          load_chunk(i + 1, c, buf + c * 32);
+          mask_max_chunk(buf + c * 32, mwn[c], mx);
+        }
       }
+      if (has_next) release_s(i + 1);
       const float l_tile = (la[0] + la[1]) + (la[2] + la[3]);
       l_run += l_tile;
       l_out += BF16 ? (lr[0] + lr[1]) + (lr[2] + lr[3]) : l_tile;
-      if (i > 0 && __any_sync(0xffffffffu, rescale_o)) {
-        // Rare: the running max rose by more than the threshold.  PV of this
-        // tile waits for p_full below, so O can be rescaled in place now.
+      if (i > 0 && __any_sync(0xffffffffu, rescale_cur)) {
+        // Rare: the running max rose by more than the threshold at tile i.
+        // Rescale O in place once the PV of tile i-1 has finished
+        // accumulating into it; the PV of tile i waits for p_full below.
+        if (C::kPBuf > 1) {
+          if (!__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&ctl.pv_done[(i - 1) % C::kPBuf]),
+                                                          ((i - 1) / C::kPBuf) & 1, abort_flag, timeout_ns)))
+            return false;
+          tc_fence_after();
+        }
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
           uint32_t u[32];
           tmem_ld32(t_lane + C::kOCol + c * 32, u);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) u[j] = __float_as_uint(__uint_as_float(u[j]) * alpha);
+          for (int j = 0; j < 32; ++j) u[j] = __float_as_uint(__uint_as_float(u[j]) * alpha_cur);
           tmem_st32(t_lane + C::kOCol + c * 32, u);
         }
       }
       tmem_wait_st();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&ctl.p_full));
-    }
+      if (lane == 0) mbar_arrive(smem_u32(&ctl.p_full[pb]));
+      if (has_next) rescale_cur = update_max(mx, alpha_cur);
+      return true;
+    };
+
+    for (uint32_t i = 0; ok && i < n; ++i) ok = step(i);
     if (!ok && lane == 0) record_abort(&ctl, err_word);
 
     // ------------------------------------------------------------ epilogue
     if (ok && n > 0) {
-      ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&ctl.pv_done), (n - 1) & 1, abort_flag, timeout_ns));
+      ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&ctl.pv_done[(n - 1) % C::kPBuf]),
+                                                      ((n - 1) / C::kPBuf) & 1, abort_flag, timeout_ns));
       if (ok) tc_fence_after();
     } else if (ok) {
       // No live tile: O is all zero; the Q buffer doubles as staging, so the
@@ -579,7 +644,7 @@ int launch_impl(const AttnParams& p, const char** msg) {
   // third resident CTA would block in tcgen05.alloc.  Registers already cap
   // residency at two; the shared-memory floor makes that independent of the
   // register count.
-  size_t smem = 1024 + C::kQBytes + C::kStages * C::kStageBytes + ((mask_bytes + 15) / 16) * 16;
+  size_t smem = C::kQBytes + C::kStages * C::kStageBytes + ((mask_bytes + 15) / 16) * 16 + sizeof(SharedCtl);
   if (smem < kMinSmemPerCta) smem = kMinSmemPerCta;
   auto kern = attn_fwd_kernel<D, BN, BF16>;
   // The dynamic shared-memory opt-in is per device; remember the largest
@@ -625,17 +690,6 @@ __global__ void wait_probe_kernel(uint32_t* err_word, uint64_t timeout_ns) {
   }
 }
 
-// Key-tile width for head dim 64: 64 by default (two S buffers in TMEM,
-// half the registers per softmax thread); SMA_ATTN_BN=128 selects the wide
-// tile (one S buffer).  Read once per process.
-int key_tile_d64() {
-  static int bn = [] {
-    const char* e = std::getenv("SMA_ATTN_BN");
-    return (e != nullptr && std::atoi(e) == 128) ? 128 : 64;
-  }();
-  return bn;
-}
-
 }  // namespace
 
 int launch_attn_fwd(const AttnParams& p, const char** msg) {
@@ -644,11 +698,7 @@ int launch_attn_fwd(const AttnParams& p, const char** msg) {
     return kErrUnsupportedN;
   }
   const bool bf = p.dtype == 1;
-  if (p.D == 64) {
-    if (key_tile_d64() == 128)
-      return bf ? launch_impl<64, 128, true>(p, msg) : launch_impl<64, 128, false>(p, msg);
-    return bf ? launch_impl<64, 64, true>(p, msg) : launch_impl<64, 64, false>(p, msg);
-  }
+  if (p.D == 64) return bf ? launch_impl<64, 64, true>(p, msg) : launch_impl<64, 64, false>(p, msg);
   if (p.D == 128) return bf ? launch_impl<128, 64, true>(p, msg) : launch_impl<128, 64, false>(p, msg);
   *msg = "attention: head dim must be 64 or 128";
   return kErrUnsupportedD;

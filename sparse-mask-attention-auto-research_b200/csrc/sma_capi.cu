@@ -118,6 +118,7 @@ int sma_device_status(void* stream, int clear) {
     if (e != cudaSuccess) return fail_cuda(e, "clear device error word");
   }
   if (v & sma::kDevErrTimeout) return fail(sma::kErrTimeout, "a device-side wait timed out");
+  if (v & sma::kDevErrLayout) return fail(sma::kErrCuda, "attention kernel: shared memory not 1024-byte aligned");
   return sma::kOk;
 }
 

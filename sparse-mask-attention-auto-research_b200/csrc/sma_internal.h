@@ -49,5 +49,6 @@ int launch_wait_probe(uint32_t* err_word, uint64_t timeout_ns, cudaStream_t stre
 
 // Device error bits.
 constexpr uint32_t kDevErrTimeout = 1u;
+constexpr uint32_t kDevErrLayout = 2u;  // shared-memory window not 1024-byte aligned
 
 }  // namespace sma
