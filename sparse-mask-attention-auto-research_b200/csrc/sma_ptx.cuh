@@ -46,11 +46,29 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
                : "memory");
 }
 
+// Potentially blocking probe: the thread may be suspended in hardware until
+// the phase completes or about `kSuspendHintNs` have passed, so waiting
+// warps do not burn the issue slots of the warps doing the work.
+constexpr uint32_t kSuspendHintNs = 100000;
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
+
+// Non-blocking probe of phase `parity`.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
       : "r"(bar), "r"(parity)
@@ -64,14 +82,12 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
                                                   volatile uint32_t* abort_flag,
                                                   uint64_t budget_ns) {
-  if (mbar_try_wait(bar, parity)) return true;
-  uint64_t t0 = global_timer_ns();
-  for (uint32_t it = 1;; ++it) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  for (;;) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0u) {
-      if (*abort_flag) return false;
-      if (global_timer_ns() - t0 > budget_ns) return false;
-    }
+    if (*abort_flag) return false;
+    if (global_timer_ns() - t0 > budget_ns) return false;
   }
 }
 
