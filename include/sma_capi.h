@@ -67,7 +67,8 @@ SMA_API int sma_pack_mask(const void* mask, void* packed, int64_t B, int64_t H, 
  * Rows with no set bit get out = 0 and lse = -FLT_MAX (the reference CUDA
  * convention, csrc/sparse_attention.cu:133,141).
  * Supported: D in {64, 128}, 1 <= N <= SMA_MAX_SEQ_LEN, 16-byte aligned
- * q/k/v/out.
+ * q/k/v/out, scale finite and > 0 (the kernels fold the scale into the
+ * exponent after the masked row max; the reference always passes 1/sqrt(D)).
  *
  * Replaces: forward()                          csrc/binding.cpp:9-47
  *           sparse_attention_fwd_fp16/_bf16()  csrc/sparse_attention.cu:149-185

@@ -698,7 +698,7 @@ int launch_attn_fwd(const AttnParams& p, const char** msg) {
     return kErrUnsupportedN;
   }
   const bool bf = p.dtype == 1;
-  if (persist_supported(p)) return launch_attn_fwd_persist(p, msg);
+  if (chain_supported(p)) return launch_attn_fwd_chain(p, msg);
   if (p.D == 64) return bf ? launch_impl<64, 64, true>(p, msg) : launch_impl<64, 64, false>(p, msg);
   if (p.D == 128) return bf ? launch_impl<128, 64, true>(p, msg) : launch_impl<128, 64, false>(p, msg);
   *msg = "attention: head dim must be 64 or 128";

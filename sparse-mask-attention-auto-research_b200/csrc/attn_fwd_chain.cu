@@ -1,0 +1,853 @@
+// Persistent two-chain fused masked-softmax attention forward, head dim 64
+// (sm_100a).
+//
+// Same computation as attn_fwd.cu (reference csrc/sparse_attention.cu:64-143):
+// O = softmax_masked(scale * Q K^T) V per (batch*head, query row); rows with
+// no set mask bit give O = 0 and lse = -FLT_MAX.
+//
+// One CTA per SM runs two independent "chains".  A chain is one softmax
+// warpgroup plus its own loader warp and MMA warp; it walks its own list of
+// work items (batch*head, 128-row query tile) and has its own Q / K / V
+// buffers in shared memory and its own S, P and O in TMEM.  Nothing couples
+// the two chains except the SM's pipes, so while one chain waits on a
+// tensor-core result, a copy or its epilogue, the other keeps the
+// exponential unit busy.
+//
+// Per chain and live 128-key tile g (tiles with no set bit in the item's
+// rows are skipped before their K/V are loaded):
+//   MMA warp:  S = Q K_g^T            (4 x tcgen05.mma M=128 N=128 K=16)
+//   softmax:   read S, mask, row max, P = 2^(S*scale*log2e - m), write P (fp16/bf16)
+//   MMA warp:  O += P V_g             (8 x tcgen05.mma M=128 N=64 K=16, P from TMEM)
+// S and P occupy separate TMEM columns: as soon as the softmax has copied S
+// into registers, the MMA warp issues Q K_{g+1}^T into the same columns, so
+// the next S is ready when the current exponentials are done.
+//
+// Warps (384 threads):
+//   0-3  softmax chain 0     4-7  softmax chain 1   (thread t of a warpgroup owns query row t)
+//        besides the softmax, each warpgroup scans the packed-mask rows of
+//        the item two ahead for live key tiles during its epilogue and
+//        publishes the list
+//   8    loader chain 0      9    loader chain 1
+//        TMA loads: Q (two buffers), K and V (two-stage rings), K one tile
+//        ahead of V so that a K copy never queues behind a V slot
+//   10   MMA chain 0 (+ TMEM allocation)   11  MMA chain 1
+//
+// TMEM (512 columns): chain c at 256c: S [0,128) | P [128,192) | O [192,256)
+// Shared memory: per chain Q[2] K[2] V[2] O-staging, 16 KiB each (224 KiB),
+// plus the control block.
+// The softmax reads its row's four mask words per tile with one 16-byte
+// global load issued a tile ahead.
+// Every wait is bounded (mbar_wait_bounded) and reports through err_word.
+#include <cfloat>
+#include <cstdio>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cudaTypedefs.h>
+
+#include "sma_internal.h"
+#include "sma_ptx.cuh"
+
+namespace sma {
+namespace {
+
+constexpr int kD = 64;
+constexpr int kBM = 128;
+constexpr int kBN = 128;
+constexpr int kThreads = 384;
+constexpr int kSlots = 4;          // live-list slots per chain
+constexpr int kMaxTiles = 64;      // N <= 8192
+constexpr int kStages = 2;         // K ring and V ring depth per chain
+constexpr int kTileBytes = kBM * kD * 2;            // 16 KiB (Q, K, V or O tile)
+constexpr int kChainBytes = (2 + 2 * kStages + 1) * kTileBytes;
+constexpr int kTmemCols = 512;
+constexpr int kChainCols = 256;
+constexpr int kSCol = 0;
+constexpr int kPCol = 128;
+constexpr int kOCol = 192;
+constexpr int kScanBatch = 4;      // 16-byte mask loads in flight per thread while scanning
+constexpr float kRescaleThreshold = 8.0f;
+constexpr float kLn2 = 0.69314718055994530942f;
+constexpr float kLog2e = 1.44269504088896340736f;
+constexpr int kMaxDevices = 64;
+
+struct ChainCtl {
+  uint64_t sched_full[kSlots];
+  uint64_t sched_empty[kSlots];  // 4 softmax warps + MMA warp + loader
+  uint64_t q_full[2];
+  uint64_t q_empty[2];
+  uint64_t k_full[kStages];
+  uint64_t k_empty[kStages];
+  uint64_t v_full[kStages];
+  uint64_t v_empty[kStages];
+  uint64_t s_full;
+  uint64_t s_free;
+  uint64_t p_full;
+  uint64_t pv_done;
+  uint64_t drain;
+  uint32_t part_lo[kSlots][4];   // per-warp live-tile bits of the item being scanned
+  uint32_t part_hi[kSlots][4];
+  uint32_t n_live[kSlots];
+  uint16_t live[kSlots][kMaxTiles];
+};
+
+struct Ctl {
+  ChainCtl ch[2];
+  uint32_t tmem_base;
+  uint32_t abort_flag;
+};
+
+constexpr size_t kSmemBytes = 2 * static_cast<size_t>(kChainBytes) + sizeof(Ctl);
+static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// Packed FP32 pairs (sm_100a f32x2 instructions): one issue slot for two lanes' worth of FMA / add.
+__device__ __forceinline__ uint64_t f2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  if constexpr (BF16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
+
+struct Item {
+  int bh, q0, rows_valid;
+};
+
+// Item w: query tiles in decreasing index order (under a causal mask the
+// last query tiles see the most keys), batch*head fastest.
+__device__ __forceinline__ Item item_of(int w, int BH, int QT, int N) {
+  Item it;
+  const int qt = QT - 1 - w / BH;
+  it.bh = w % BH;
+  it.q0 = qt * kBM;
+  it.rows_valid = min(kBM, N - it.q0);
+  return it;
+}
+
+// Bits of word `cw` of a packed-mask row that address columns < N.
+__device__ __forceinline__ uint32_t valid_bits(int cw, int N) {
+  const int valid = N - cw * 32;
+  return valid >= 32 ? 0xFFFFFFFFu : (valid <= 0 ? 0u : ((1u << valid) - 1u));
+}
+
+// The four mask words of key tile kt for one query row, columns >= N cleared.
+__device__ __forceinline__ void load_tile_words(const uint32_t* mrow, int kt, int W, int N, bool vec,
+                                                uint32_t (&mw)[4]) {
+  if (vec) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(mrow + kt * 4));
+    mw[0] = v.x;
+    mw[1] = v.y;
+    mw[2] = v.z;
+    mw[3] = v.w;
+  } else {
+#pragma unroll
+    for (int w = 0; w < 4; ++w) mw[w] = (kt * 4 + w < W) ? __ldg(mrow + kt * 4 + w) : 0u;
+  }
+  if (N - kt * kBN < kBN) {
+#pragma unroll
+    for (int w = 0; w < 4; ++w) mw[w] &= valid_bits(kt * 4 + w, N);
+  }
+}
+
+__device__ __forceinline__ void set_live(int g, uint32_t x, uint32_t& lo, uint32_t& hi) {
+  if (x != 0u) {
+    if (g < 32) lo |= 1u << g;
+    else hi |= 1u << (g - 32);
+  }
+}
+
+// OR of the four words of 16-byte group g (key tile g), columns >= N cleared.
+__device__ __forceinline__ uint32_t group_or(const uint4& v, int g, int N) {
+  if (N - g * kBN >= kBN) return v.x | v.y | v.z | v.w;
+  return (v.x & valid_bits(g * 4, N)) | (v.y & valid_bits(g * 4 + 1, N)) | (v.z & valid_bits(g * 4 + 2, N)) |
+         (v.w & valid_bits(g * 4 + 3, N));
+}
+
+// Position of one chain in the flattened sequence of its live tiles.
+struct Cursor {
+  int i;       // item index (-1 before the first item, n_items when exhausted)
+  uint32_t t;  // live tile within the item
+  uint32_t n;  // live tiles of item i
+};
+
+template <bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_fwd_chain_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                          const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                          const uint32_t* __restrict__ mask, float* __restrict__ lse, int N, int BH, int W,
+                          int KT, int total_items, int vec, float scale_log2, uint32_t* err_word,
+                          uint64_t timeout_ns) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t base = smem_u32(smem);
+  if ((base & 1023u) != 0u) {
+    if (threadIdx.x == 0) atomicOr(err_word, kDevErrLayout);
+    return;
+  }
+  Ctl& ctl = *reinterpret_cast<Ctl*>(smem + 2 * kChainBytes);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int QT = (N + kBM - 1) / kBM;
+  const int G = gridDim.x;
+  volatile uint32_t* abort_flag = &ctl.abort_flag;
+
+  // The 2G chains (chain c of CTA b is k = c*G + b) take the items round by
+  // round, serpentine: in round i chain k takes item 2G*i + k (i even) or
+  // 2G*i + 2G-1-k (i odd), which evens out per-SM work when item sizes fall
+  // with the item index (causal masks).
+  auto chain_item = [&](int c, int i) {
+    const int k = c * G + static_cast<int>(blockIdx.x);
+    return 2 * G * i + ((i & 1) ? 2 * G - 1 - k : k);
+  };
+  auto chain_items = [&](int c) {
+    const int k = c * G + static_cast<int>(blockIdx.x);
+    const int full = total_items / (2 * G), rem = total_items % (2 * G);
+    const int off = (full & 1) ? 2 * G - 1 - k : k;
+    return full + (off < rem ? 1 : 0);
+  };
+
+  if (threadIdx.x == 256) {
+    for (int c = 0; c < 2; ++c) {
+      ChainCtl& cc = ctl.ch[c];
+      for (int s = 0; s < kSlots; ++s) {
+        mbar_init(smem_u32(&cc.sched_full[s]), 1);
+        mbar_init(smem_u32(&cc.sched_empty[s]), 6);
+      }
+      for (int b = 0; b < 2; ++b) {
+        mbar_init(smem_u32(&cc.q_full[b]), 1);
+        mbar_init(smem_u32(&cc.q_empty[b]), 1);
+      }
+      for (int s = 0; s < kStages; ++s) {
+        mbar_init(smem_u32(&cc.k_full[s]), 1);
+        mbar_init(smem_u32(&cc.k_empty[s]), 1);
+        mbar_init(smem_u32(&cc.v_full[s]), 1);
+        mbar_init(smem_u32(&cc.v_empty[s]), 1);
+      }
+      mbar_init(smem_u32(&cc.s_full), 1);
+      mbar_init(smem_u32(&cc.s_free), 4);
+      mbar_init(smem_u32(&cc.p_full), 4);
+      mbar_init(smem_u32(&cc.pv_done), 1);
+      mbar_init(smem_u32(&cc.drain), 1);
+    }
+    ctl.abort_flag = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 10) {
+    tmem_alloc(smem_u32(&ctl.tmem_base), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl.tmem_base;
+
+  auto fail = [&]() {
+    ctl.abort_flag = 1;
+    atomicOr(err_word, kDevErrTimeout);
+  };
+
+  // Moves a cursor to the next live tile (one thread): 1 = found, 0 = no
+  // tiles left, -1 = a wait gave up.  With `release`, the cursor arrives on
+  // sched_empty of every item it leaves.
+  auto advance = [&](ChainCtl& cc, Cursor& cu, int n_items, bool release) -> int {
+    if (cu.i >= 0 && cu.i < n_items && cu.t + 1 < cu.n) {
+      ++cu.t;
+      return 1;
+    }
+    if (release && cu.i >= 0 && cu.i < n_items) mbar_arrive(smem_u32(&cc.sched_empty[cu.i % kSlots]));
+    for (int i = cu.i + 1; i < n_items; ++i) {
+      const int slot = i % kSlots;
+      if (!mbar_wait_bounded(smem_u32(&cc.sched_full[slot]), (i / kSlots) & 1, abort_flag, timeout_ns)) return -1;
+      const uint32_t n = cc.n_live[slot];
+      if (n == 0) {
+        if (release) mbar_arrive(smem_u32(&cc.sched_empty[slot]));
+        continue;
+      }
+      cu.i = i;
+      cu.t = 0;
+      cu.n = n;
+      return 1;
+    }
+    cu.i = n_items;
+    return 0;
+  };
+
+  if (warp == 8 || warp == 9) {
+    // ================================================================ loader
+    const int c = warp - 8;
+    ChainCtl& cc = ctl.ch[c];
+    if (lane == 0) {
+      const uint32_t sQ = base + c * kChainBytes;
+      const uint32_t sK = sQ + 2 * kTileBytes;
+      const uint32_t sV = sK + kStages * kTileBytes;
+      const int n_items = chain_items(c);
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_o);
+      Cursor kc{-1, 0u, 0u}, vc{-1, 0u, 0u};
+      uint32_t gk = 0, gv = 0, q_count = 0;  // K, V and Q copies issued
+      bool ok = true;
+      auto issue_k = [&]() -> bool {
+        const Item it = item_of(chain_item(c, kc.i), BH, QT, N);
+        if (kc.t == 0) {
+          // First tile of an item: its Q, into the buffer the item two back used.
+          const int qb = q_count & 1;
+          if (q_count >= 2 &&
+              !mbar_wait_bounded(smem_u32(&cc.q_empty[qb]), ((q_count - 2) >> 1) & 1, abort_flag, timeout_ns))
+            return false;
+          mbar_arrive_expect_tx(smem_u32(&cc.q_full[qb]), kTileBytes);
+          tma_load_3d(sQ + qb * kTileBytes, &tm_q, smem_u32(&cc.q_full[qb]), 0, it.q0, it.bh);
+          ++q_count;
+        }
+        const int stage = gk % kStages;
+        if (gk >= static_cast<uint32_t>(kStages) &&
+            !mbar_wait_bounded(smem_u32(&cc.k_empty[stage]), ((gk / kStages) - 1) & 1, abort_flag, timeout_ns))
+          return false;
+        const int kt = cc.live[kc.i % kSlots][kc.t];
+        mbar_arrive_expect_tx(smem_u32(&cc.k_full[stage]), kTileBytes);
+        tma_load_3d(sK + stage * kTileBytes, &tm_k, smem_u32(&cc.k_full[stage]), 0, kt * kBN, it.bh);
+        ++gk;
+        return true;
+      };
+      auto issue_v = [&]() -> bool {
+        const Item it = item_of(chain_item(c, vc.i), BH, QT, N);
+        const int stage = gv % kStages;
+        if (gv >= static_cast<uint32_t>(kStages) &&
+            !mbar_wait_bounded(smem_u32(&cc.v_empty[stage]), ((gv / kStages) - 1) & 1, abort_flag, timeout_ns))
+          return false;
+        const int kt = cc.live[vc.i % kSlots][vc.t];
+        mbar_arrive_expect_tx(smem_u32(&cc.v_full[stage]), kTileBytes);
+        tma_load_3d(sV + stage * kTileBytes, &tm_v, smem_u32(&cc.v_full[stage]), 0, kt * kBN, it.bh);
+        ++gv;
+        return true;
+      };
+      int rk = advance(cc, kc, n_items, false);
+      if (rk < 0 || (rk == 1 && !issue_k())) ok = false;
+      while (ok) {
+        const int rv = advance(cc, vc, n_items, true);
+        if (rv <= 0) {
+          ok = rv == 0;
+          break;
+        }
+        if (rk == 1) {
+          rk = advance(cc, kc, n_items, false);
+          if (rk < 0 || (rk == 1 && !issue_k())) {
+            ok = false;
+            break;
+          }
+        }
+        if (!issue_v()) {
+          ok = false;
+          break;
+        }
+      }
+      if (!ok) {
+        fail();
+        // Let the copies this thread started land before the CTA exits.
+        uint32_t zero = 0;
+        for (uint32_t x = (gk > static_cast<uint32_t>(kStages) ? gk - kStages : 0u); x < gk; ++x)
+          mbar_wait_bounded(smem_u32(&cc.k_full[x % kStages]), (x / kStages) & 1, &zero, timeout_ns);
+        for (uint32_t x = (gv > static_cast<uint32_t>(kStages) ? gv - kStages : 0u); x < gv; ++x)
+          mbar_wait_bounded(smem_u32(&cc.v_full[x % kStages]), (x / kStages) & 1, &zero, timeout_ns);
+        for (uint32_t q = (q_count > 2 ? q_count - 2 : 0u); q < q_count; ++q)
+          mbar_wait_bounded(smem_u32(&cc.q_full[q & 1]), (q >> 1) & 1, &zero, timeout_ns);
+      }
+    }
+  } else if (warp == 10 || warp == 11) {
+    // ================================================================ MMA issuer
+    const int c = warp - 10;
+    ChainCtl& cc = ctl.ch[c];
+    if (lane == 0) {
+      const uint32_t sQ = base + c * kChainBytes;
+      const uint32_t sK = sQ + 2 * kTileBytes;
+      const uint32_t sV = sK + kStages * kTileBytes;
+      const uint32_t tS = tmem + c * kChainCols + kSCol;
+      const uint32_t tP = tmem + c * kChainCols + kPCol;
+      const uint32_t tO = tmem + c * kChainCols + kOCol;
+      constexpr uint32_t idesc_qk = make_idesc_f16(kBM, kBN, BF16 ? 1 : 0, 0);
+      constexpr uint32_t idesc_pv = make_idesc_f16(kBM, kD, BF16 ? 1 : 0, 1);
+      const int n_items = chain_items(c);
+      bool ok = true;
+
+      Cursor qc{-1, 0u, 0u};  // next tile to multiply by K^T
+      uint32_t q_count = 0;
+      int qqb = 0;            // Q buffer of the cursor's item
+      auto advance_qk = [&]() -> int {
+        const int res = advance(cc, qc, n_items, true);
+        if (res == 1 && qc.t == 0) {
+          qqb = q_count & 1;
+          if (!mbar_wait_bounded(smem_u32(&cc.q_full[qqb]), (q_count >> 1) & 1, abort_flag, timeout_ns))
+            return -1;
+          ++q_count;
+        }
+        return res;
+      };
+      bool first_of[2] = {false, false};  // tile g is the first of its item (O overwritten)
+      auto issue_qk = [&](uint32_t g) -> bool {
+        const int stage = g % kStages;
+        if (!mbar_wait_bounded(smem_u32(&cc.k_full[stage]), (g / kStages) & 1, abort_flag, timeout_ns))
+          return false;
+        // S is free once the softmax has copied S of tile g-1 into registers.
+        if (g > 0 && !mbar_wait_bounded(smem_u32(&cc.s_free), (g - 1) & 1, abort_flag, timeout_ns)) return false;
+        tc_fence_after();
+        const uint32_t sQb = sQ + qqb * kTileBytes;
+        const uint32_t sKb = sK + stage * kTileBytes;
+#pragma unroll
+        for (int kk = 0; kk < kD / 16; ++kk)
+          mma_ss(tS, smem_desc_sw128(sQb + kk * 32, 16, 1024), smem_desc_sw128(sKb + kk * 32, 16, 1024), idesc_qk,
+                 kk > 0 ? 1u : 0u);
+        mma_commit(smem_u32(&cc.s_full));
+        mma_commit(smem_u32(&cc.k_empty[stage]));
+        if (qc.t + 1 == qc.n) mma_commit(smem_u32(&cc.q_empty[qqb]));  // last QK^T of the item
+        first_of[g & 1] = (qc.t == 0);
+        return true;
+      };
+
+      uint32_t n_qk = 0;
+      int res = advance_qk();
+      if (res < 0 || (res == 1 && !issue_qk(0))) ok = false;
+      if (ok && res == 1) n_qk = 1;
+      for (uint32_t g = 0; ok && g < n_qk; ++g) {
+        res = advance_qk();
+        if (res < 0 || (res == 1 && !issue_qk(g + 1))) {
+          ok = false;
+          break;
+        }
+        if (res == 1) ++n_qk;
+        const int stage = g % kStages;
+        if (!mbar_wait_bounded(smem_u32(&cc.p_full), g & 1, abort_flag, timeout_ns) ||
+            !mbar_wait_bounded(smem_u32(&cc.v_full[stage]), (g / kStages) & 1, abort_flag, timeout_ns)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sVb = sV + stage * kTileBytes;
+        const bool fresh = first_of[g & 1];
+#pragma unroll
+        for (int kk = 0; kk < kBN / 16; ++kk)
+          mma_ts(tO, tP + kk * 8, smem_desc_sw128(sVb + kk * 2048, kBN * 128, 1024), idesc_pv,
+                 (fresh && kk == 0) ? 0u : 1u);
+        mma_commit(smem_u32(&cc.pv_done));
+        mma_commit(smem_u32(&cc.v_empty[stage]));
+      }
+      if (!ok) fail();
+      // Every MMA this thread issued must complete before TMEM is released.
+      mma_commit(smem_u32(&cc.drain));
+      uint32_t zero = 0;
+      mbar_wait_bounded(smem_u32(&cc.drain), 0, &zero, timeout_ns);
+    }
+  } else {
+    // ================================================================ softmax
+    const int c = warp >> 2;
+    const int wq = warp & 3;
+    ChainCtl& cc = ctl.ch[c];
+    const int r = threadIdx.x & 127;  // query row == TMEM lane
+    const uint32_t t_lane = tmem + c * kChainCols + (static_cast<uint32_t>(wq * 32) << 16);
+    const uint32_t sO = base + c * kChainBytes + (2 + 2 * kStages) * kTileBytes;
+    uint8_t* out_row = smem + c * kChainBytes + (2 + 2 * kStages) * kTileBytes + r * 128;
+    const int n_items = chain_items(c);
+    const int bar_id = 1 + c;
+    const int G4 = W >> 2;  // 16-byte groups per mask row (vec path: one per key tile)
+    bool ok = true;
+    uint32_t g = 0;  // tiles processed by this chain
+
+    auto wait_all = [&](uint64_t& bar, uint32_t parity) -> bool {
+      const bool all =
+          __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&bar), parity, abort_flag, timeout_ns));
+      if (all) tc_fence_after();
+      return all;
+    };
+    auto arrive_warp = [&](uint64_t& bar) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bar));
+    };
+    auto row_ptr = [&](const Item& it) {
+      return mask + (static_cast<int64_t>(it.bh) * N + it.q0 + r) * W;
+    };
+    // Mask words of key tile kt for this thread's row of `it` (0 for padding rows).
+    auto fetch_words = [&](const Item& it, int kt, uint32_t (&mw)[4]) {
+      if (r < it.rows_valid) {
+        load_tile_words(row_ptr(it), kt, W, N, vec != 0, mw);
+      } else {
+        mw[0] = mw[1] = mw[2] = mw[3] = 0u;
+      }
+    };
+    // Live-tile bits of this thread's row of item j, from the 16-byte groups
+    // at index >= g0 (groups below g0 were OR-ed by the caller).
+    auto scan_rest = [&](const Item& it, int g0, uint32_t& lo, uint32_t& hi) {
+      if (r >= it.rows_valid) return;
+      const uint32_t* mrow = row_ptr(it);
+      if (vec) {
+        for (int gb = g0; gb < G4; gb += kScanBatch) {
+          uint4 v[kScanBatch];
+#pragma unroll
+          for (int u = 0; u < kScanBatch; ++u)
+            v[u] = (gb + u < G4) ? __ldg(reinterpret_cast<const uint4*>(mrow) + gb + u) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+          for (int u = 0; u < kScanBatch; ++u) set_live(gb + u, group_or(v[u], gb + u, N), lo, hi);
+        }
+      } else {
+        for (int cw = g0 * 4; cw < W; ++cw) set_live(cw >> 2, __ldg(mrow + cw) & valid_bits(cw, N), lo, hi);
+      }
+    };
+    // Stores this warp's share of item j's live bits (before a WG barrier).
+    auto post_part = [&](int j, uint32_t lo, uint32_t hi) {
+      lo = __reduce_or_sync(0xffffffffu, lo);
+      hi = __reduce_or_sync(0xffffffffu, hi);
+      if (lane == 0) {
+        cc.part_lo[j % kSlots][wq] = lo;
+        cc.part_hi[j % kSlots][wq] = hi;
+      }
+    };
+    // Thread 0 of the WG, after a WG barrier: builds item j's live list and publishes it.
+    auto publish = [&](int j) {
+      const int slot = j % kSlots;
+      if (j >= kSlots &&
+          !mbar_wait_bounded(smem_u32(&cc.sched_empty[slot]), ((j / kSlots) - 1) & 1, abort_flag, timeout_ns)) {
+        fail();
+        return;
+      }
+      const uint32_t lo = cc.part_lo[slot][0] | cc.part_lo[slot][1] | cc.part_lo[slot][2] | cc.part_lo[slot][3];
+      const uint32_t hi = cc.part_hi[slot][0] | cc.part_hi[slot][1] | cc.part_hi[slot][2] | cc.part_hi[slot][3];
+      uint32_t n = 0;
+      for (int t = 0; t < KT; ++t) {
+        const uint32_t bit = t < 32 ? (lo >> t) & 1u : (hi >> (t - 32)) & 1u;
+        if (bit) cc.live[slot][n++] = static_cast<uint16_t>(t);
+      }
+      cc.n_live[slot] = n;
+      mbar_arrive(smem_u32(&cc.sched_full[slot]));
+    };
+
+    // Prologue: the live lists of the first two items.
+    const int n_pre = n_items < 2 ? n_items : 2;
+    for (int j = 0; j < n_pre; ++j) {
+      uint32_t lo = 0u, hi = 0u;
+      scan_rest(item_of(chain_item(c, j), BH, QT, N), 0, lo, hi);
+      post_part(j, lo, hi);
+    }
+    named_bar_sync(bar_id, 128);
+    if (r == 0)
+      for (int j = 0; j < n_pre; ++j) publish(j);
+
+    uint32_t mw[4] = {0u, 0u, 0u, 0u};
+    bool have_mw = false;  // mw already holds tile 0 of the current item
+    for (int i = 0; i < n_items; ++i) {
+      const int slot = i % kSlots;
+      const Item it = item_of(chain_item(c, i), BH, QT, N);
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&cc.sched_full[slot]), (i / kSlots) & 1,
+                                                              abort_flag, timeout_ns));
+      const uint32_t n = ok ? cc.n_live[slot] : 0u;
+      if (n > 0 && !have_mw) fetch_words(it, cc.live[slot][0], mw);
+      have_mw = false;
+      float m_run = -INFINITY, l_run = 0.f, l_out = 0.f;
+
+      for (uint32_t t = 0; ok && t < n; ++t, ++g) {
+        // At the last tile, look up the next item's first live tile (its
+        // list was published an item ago) so its mask words can be fetched early.
+        int next_kt = -1;
+        if (t + 1 == n && i + 1 < n_items) {
+          const int slot2 = (i + 1) % kSlots;
+          if (__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&cc.sched_full[slot2]), ((i + 1) / kSlots) & 1,
+                                                         abort_flag, timeout_ns)) &&
+              cc.n_live[slot2] > 0)
+            next_kt = cc.live[slot2][0];
+        }
+        if (!wait_all(cc.s_full, g & 1)) {
+          ok = false;
+          break;
+        }
+        float s[kBN];
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) tmem_ld32f(t_lane + kSCol + ch * 32, s + ch * 32);
+        tmem_wait_ld();
+        arrive_warp(cc.s_free);  // the next QK^T may overwrite S now
+
+        float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          const uint32_t word = mw[ch];
+#pragma unroll
+          for (int jj = 0; jj < 32; jj += 2) {
+            const float v0 = (word & (1u << jj)) ? s[ch * 32 + jj] : -INFINITY;
+            const float v1 = (word & (2u << jj)) ? s[ch * 32 + jj + 1] : -INFINITY;
+            s[ch * 32 + jj] = v0;
+            s[ch * 32 + jj + 1] = v1;
+            mx[(jj >> 1) & 3] = max3f(mx[(jj >> 1) & 3], v0, v1);
+          }
+        }
+        // The next tile's mask words, a whole tile of exponentials ahead of their use.
+        if (t + 1 < n) {
+          fetch_words(it, cc.live[slot][t + 1], mw);
+        } else if (next_kt >= 0) {
+          fetch_words(item_of(chain_item(c, i + 1), BH, QT, N), next_kt, mw);
+          have_mw = true;
+        }
+
+        // Lazy rescale: the running max only moves when it rises by more than
+        // the threshold, so O needs correcting rarely.
+        const float x_max = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale_log2;
+        float alpha = 1.f;
+        bool rescale = false;
+        if (x_max > m_run + kRescaleThreshold) {
+          if (m_run != -INFINITY) {
+            alpha = ex2f(m_run - x_max);
+            rescale = true;
+          }
+          l_run *= alpha;
+          l_out *= alpha;
+          m_run = x_max;
+        }
+        // P (single buffer) was last read by the PV of tile g-1.
+        if (g > 0 && !wait_all(cc.pv_done, (g - 1) & 1)) {
+          ok = false;
+          break;
+        }
+        const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+        const uint64_t scale2 = f2(scale_log2, scale_log2);
+        const uint64_t negm2 = f2(-m_use, -m_use);
+        float la[2] = {0.f, 0.f};
+        uint64_t lr2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
+#pragma unroll
+        for (int ch = 0; ch < 4; ++ch) {
+          uint32_t pk[16];
+#pragma unroll
+          for (int jj = 0; jj < 16; ++jj) {
+            float x0, x1;
+            f2_split(fma2(f2(s[ch * 32 + 2 * jj], s[ch * 32 + 2 * jj + 1]), scale2, negm2), x0, x1);
+            const float p0 = ex2f(x0);
+            const float p1 = ex2f(x1);
+            pk[jj] = pack2<BF16>(p0, p1);
+            la[jj & 1] += p0 + p1;
+            if constexpr (BF16) {
+              lr2[jj & 1] = add2(lr2[jj & 1], f2(__uint_as_float(pk[jj] << 16), __uint_as_float(pk[jj] & 0xFFFF0000u)));
+            }
+          }
+          tmem_st16(t_lane + kPCol + ch * 16, pk);
+        }
+        float lr[2];
+        f2_split(add2(lr2[0], lr2[1]), lr[0], lr[1]);
+        if (__any_sync(0xffffffffu, rescale)) {
+          // Rare: the running max rose by more than the threshold; bring O
+          // (PV of tiles before g, complete) to the new max before PV of g.
+#pragma unroll 1
+          for (int ch = 0; ch < kD / 16; ++ch) {
+            uint32_t u[16];
+            tmem_ld16(t_lane + kOCol + ch * 16, u);
+            tmem_wait_ld();
+#pragma unroll
+            for (int q = 0; q < 16; ++q) u[q] = __float_as_uint(__uint_as_float(u[q]) * alpha);
+            tmem_st16(t_lane + kOCol + ch * 16, u);
+          }
+        }
+        tmem_wait_st();
+        arrive_warp(cc.p_full);
+        const float l_tile = la[0] + la[1];
+        l_run += l_tile;
+        l_out += BF16 ? lr[0] + lr[1] : l_tile;
+      }
+      // This item's live list is no longer read.
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&cc.sched_empty[slot]));
+
+      // ------------------------------------------------------------ epilogue
+      // Scan of item i+2: its mask rows are prefetched into L1 before the
+      // wait for the last PV, so the loads after it hit (a prefetch holds no
+      // registers).
+      const bool do_scan = i + 2 < n_items;
+      const Item itn = item_of(chain_item(c, do_scan ? i + 2 : i), BH, QT, N);
+      if (do_scan && r < itn.rows_valid) {
+        const uintptr_t a0 = reinterpret_cast<uintptr_t>(row_ptr(itn));
+        const uintptr_t a1 = a0 + static_cast<uintptr_t>(W) * 4u;
+        for (uintptr_t a = a0 & ~static_cast<uintptr_t>(127); a < a1; a += 128)
+          asm volatile("prefetch.global.L1 [%0];" ::"l"(a));
+      }
+      // O of the item, normalised and packed to 16-bit pairs (32 words per row).
+      const float inv = (l_out > 0.f) ? (1.f / l_out) : 0.f;
+      uint32_t h[32];
+      if (ok && n > 0 && wait_all(cc.pv_done, (g - 1) & 1)) {
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          uint32_t u[32];
+          tmem_ld32(t_lane + kOCol + half * 32, u);
+          tmem_wait_ld();
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            h[half * 16 + e] = pack2<BF16>(__uint_as_float(u[2 * e]) * inv, __uint_as_float(u[2 * e + 1]) * inv);
+        }
+      } else {
+        if (n > 0) ok = false;
+#pragma unroll
+        for (int e = 0; e < 32; ++e) h[e] = 0u;
+      }
+      if (do_scan) {
+        uint32_t lo = 0u, hi = 0u;
+        scan_rest(itn, 0, lo, hi);
+        post_part(i + 2, lo, hi);
+      }
+      // The previous item's O store must have finished reading the staging tile.
+      if (r == 0) bulk_wait_group_read0();
+      named_bar_sync(bar_id, 128);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int chunk = q ^ (r & 7);  // 128-byte swizzle of the O tensor map
+        *reinterpret_cast<uint4*>(out_row + chunk * 16) = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
+      }
+      if (lse != nullptr && r < it.rows_valid)
+        lse[static_cast<int64_t>(it.bh) * N + it.q0 + r] = (l_run > 0.f) ? (m_run + log2f(l_run)) * kLn2 : -FLT_MAX;
+      fence_proxy_async_smem();
+      named_bar_sync(bar_id, 128);
+      if (r == 0) {
+        if (ctl.abort_flag == 0) {
+          tma_store_3d(&tm_o, sO, 0, it.q0, it.bh);
+          bulk_commit_group();
+        }
+        if (do_scan) publish(i + 2);
+      }
+    }
+    if (!ok && lane == 0) fail();
+    if (r == 0) bulk_wait_group_read0();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 10) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// [BH, N, 64] view of a contiguous [B, H, N, 64] tensor, 128-row boxes, 128-byte swizzle.
+bool map3d(CUtensorMap* m, const void* ptr, int dtype, int64_t BH, int64_t N) {
+  auto fn = encode_fn();
+  if (fn == nullptr) return false;
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(BH)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(kD * 2), static_cast<cuuint64_t>(N * kD * 2)};
+  cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(kBM), 1u};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  return fn(m, dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+            const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <bool BF16>
+int launch(const AttnParams& p, const char** msg) {
+  const int64_t BH = p.B * p.H;
+  const int64_t N = p.N;
+  const int64_t W = (N + 31) / 32;
+  const int64_t KT = (N + kBN - 1) / kBN;
+  const int64_t QT = (N + kBM - 1) / kBM;
+  const int64_t total = QT * BH;
+  if (total > 0x3FFFFFFFll) {
+    *msg = "attention: batch*heads too large";
+    return kErrArg;
+  }
+  CUtensorMap mq, mk, mv, mo;
+  if (!map3d(&mq, p.q, p.dtype, BH, N) || !map3d(&mk, p.k, p.dtype, BH, N) || !map3d(&mv, p.v, p.dtype, BH, N) ||
+      !map3d(&mo, p.out, p.dtype, BH, N)) {
+    *msg = "attention: cuTensorMapEncodeTiled failed (pointer alignment or driver entry point)";
+    return kErrCuda;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    *msg = "attention: no current CUDA device";
+    return kErrCuda;
+  }
+  static int sms[kMaxDevices] = {};
+  static bool smem_set[kMaxDevices] = {};
+  if (sms[dev] == 0 && cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    *msg = "attention: cannot query the SM count";
+    return kErrCuda;
+  }
+  auto kern = attn_fwd_chain_kernel<BF16>;
+  if (!smem_set[dev]) {
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+    if (e != cudaSuccess) {
+      *msg = cudaGetErrorString(e);
+      return kErrLaunch;
+    }
+    smem_set[dev] = true;
+  }
+  const int vec = (W % 4 == 0 && (reinterpret_cast<uintptr_t>(p.mask) & 15u) == 0) ? 1 : 0;
+  const int grid = static_cast<int>(total < sms[dev] ? total : sms[dev]);
+  kern<<<grid, kThreads, kSmemBytes, p.stream>>>(mq, mk, mv, mo, p.mask, p.lse, static_cast<int>(N),
+                                                 static_cast<int>(BH), static_cast<int>(W), static_cast<int>(KT),
+                                                 static_cast<int>(total), vec, p.scale * kLog2e, p.err_word,
+                                                 p.timeout_ns);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    static thread_local char buf[256];
+    cudaFuncAttributes fa{};
+    cudaFuncGetAttributes(&fa, kern);
+    snprintf(buf, sizeof(buf), "%s (chain kernel: %d threads, %d regs/thread, max %d threads/block, %zu B dynamic smem)",
+             cudaGetErrorString(e), kThreads, fa.numRegs, fa.maxThreadsPerBlock, kSmemBytes);
+    *msg = buf;
+    return kErrLaunch;
+  }
+  return kOk;
+}
+
+}  // namespace
+
+bool chain_supported(const AttnParams& p) { return p.D == kD && p.N <= kMaxTiles * kBN; }
+
+int launch_attn_fwd_chain(const AttnParams& p, const char** msg) {
+  return p.dtype == 1 ? launch<true>(p, msg) : launch<false>(p, msg);
+}
+
+}  // namespace sma

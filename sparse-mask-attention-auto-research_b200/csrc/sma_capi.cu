@@ -72,6 +72,7 @@ int sma_attn_fwd(int dtype, const void* q, const void* k, const void* v, const v
   if (D != 64 && D != 128) return fail(sma::kErrUnsupportedD, "attention: head dim must be 64 or 128");
   if (N > SMA_MAX_SEQ_LEN)
     return fail(sma::kErrUnsupportedN, "attention: sequence length above the supported maximum (8192)");
+  if (!(scale > 0.f) || !(scale < INFINITY)) return fail(sma::kErrArg, "attention: scale must be finite and > 0");
   if (B == 0 || H == 0 || N == 0) return sma::kOk;
   if (!q || !k || !v || !mask_packed || !out) return fail(sma::kErrArg, "attention: null pointer");
   if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out))

@@ -42,10 +42,10 @@ int launch_pack_mask(const uint8_t* mask, uint32_t* packed, int64_t rows, int64_
 
 int launch_attn_fwd(const AttnParams& p, const char** msg);
 
-// Persistent one-CTA-per-SM kernel (attn_fwd_persist.cu): head dim 64 and
-// N <= 2048.  launch_attn_fwd dispatches to it when persist_supported().
-bool persist_supported(const AttnParams& p);
-int launch_attn_fwd_persist(const AttnParams& p, const char** msg);
+// Persistent two-chain kernel (attn_fwd_chain.cu): head dim 64, any
+// supported N.  launch_attn_fwd dispatches to it when chain_supported().
+bool chain_supported(const AttnParams& p);
+int launch_attn_fwd_chain(const AttnParams& p, const char** msg);
 
 // Launches one CTA that waits on an mbarrier nothing ever arrives on, using
 // the same bounded-wait helper as the attention kernel; it must give up after

@@ -44,8 +44,8 @@ def test_abi_version(lib):
     assert lib.sma_abi_version() == 1
 
 
-def _attn(lib, dtype=0, q=16, k=16, v=16, m=16, o=16, lse=None, B=1, H=1, N=64, D=64):
-    return lib.sma_attn_fwd(dtype, q, k, v, m, o, lse, B, H, N, D, 0.125, None)
+def _attn(lib, dtype=0, q=16, k=16, v=16, m=16, o=16, lse=None, B=1, H=1, N=64, D=64, scale=0.125):
+    return lib.sma_attn_fwd(dtype, q, k, v, m, o, lse, B, H, N, D, scale, None)
 
 
 def test_attn_rejects_bad_dtype(lib):
@@ -67,6 +67,12 @@ def test_attn_rejects_bad_args(lib):
     assert _attn(lib, q=None) == L.SMA_ERR_ARG
     assert _attn(lib, q=8) == L.SMA_ERR_ARG  # not 16-byte aligned
     assert b"aligned" in lib.sma_last_error()
+
+
+def test_attn_rejects_bad_scale(lib):
+    for bad in (0.0, -0.125, float("inf"), float("nan")):
+        assert _attn(lib, scale=bad) == L.SMA_ERR_ARG
+        assert b"scale" in lib.sma_last_error()
 
 
 def test_empty_problems_are_noops(lib):
