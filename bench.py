@@ -375,6 +375,8 @@ def run_ours(args):
         return 0
 
     peaks = load_peaks()
+    # D = 64: the persistent two-chain kernel; D = 128: the two-CTA-per-SM kernel.
+    attn_kernel = "attn_fwd_chain_kernel" if D == 64 else "attn_fwd_kernel"
     bm, bn = workloads.kernel_tile(D)
     live = workloads.live_tile_fraction(m, bm, bn)
     a_bytes = workloads.attn_bytes(lb, lh, N, D)
@@ -404,8 +406,8 @@ def run_ours(args):
                    "parallelism": f"bh-shard{world}" if world > 1 else "single",
                    "l2": "flushed (512 MiB memset) before every timed step"},
         "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peaks["hbm_gbs"], "unit": "GB/s",
-                     "frac": achieved_gbs / peaks["hbm_gbs"], "traffic": load_traffic("attn_fwd", args.config),
-                     "kernel": "attn_fwd_kernel", "algorithmic_bytes_per_launch": a_bytes,
+                     "frac": achieved_gbs / peaks["hbm_gbs"], "traffic": load_traffic(attn_kernel, args.config),
+                     "kernel": attn_kernel, "algorithmic_bytes_per_launch": a_bytes,
                      "avg_launch_ms": mean_attn, "peak_source": peaks["source"]},
         "roofline_tensor": {"achieved": tflops_live, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                             "frac": tflops_live / peaks["bf16_tflops"], "live_tile_fraction": live,
