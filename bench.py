@@ -239,6 +239,7 @@ def run_ours(args):
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 under torchrun")
     from python import SparseAttentionFunction, pack_mask, sparse_attention, sparse_attn_cuda, workloads
+    from python.sparse_attention import _pack_for_attention as pack_for_attention
 
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
@@ -268,10 +269,10 @@ def run_ours(args):
         # (python/sparse_attention.py), split by an event between the two kernels.
         if evs:
             evs[0].record(stream)
-        packed = pack_mask(m)
+        packed, occupancy = pack_for_attention(m, D)
         if evs:
             evs[1].record(stream)
-        out = SparseAttentionFunction.apply(q, k, v, packed, m, scale, N)
+        out = SparseAttentionFunction.apply(q, k, v, packed, m, scale, N, occupancy)
         if evs:
             evs[2].record(stream)
         return out

@@ -79,6 +79,31 @@ SMA_API int sma_attn_fwd(int dtype, const void* q, const void* k, const void* v,
                  void* stream);
 
 /*
+ * Fused bool -> bit packing plus occupancy map.  Writes `packed` exactly as
+ * sma_pack_mask does and `occupancy`: uint32 [B*H, ceil(N/128), 2], where bit t
+ * of the pair for (batch*head, query tile qt) is set iff key tile t (keys
+ * 128t .. 128t+127) has a set mask bit in query rows 128qt .. 128qt+127.
+ * Needs N % 32 == 0, N <= SMA_MAX_SEQ_LEN, a 16-byte aligned mask and 4-byte
+ * aligned outputs (SMA_ERR_ARG / SMA_ERR_UNSUPPORTED_N otherwise; callers
+ * then use sma_pack_mask).  The packer reads every mask byte anyway, so the
+ * map costs no extra HBM pass.
+ * No reference counterpart: the reference's attention re-tests every mask bit.
+ */
+SMA_API int sma_pack_mask_occupancy(const void* mask, void* packed, void* occupancy, int64_t B, int64_t H,
+                                    int64_t N, void* stream);
+
+/*
+ * sma_attn_fwd with the occupancy map written by sma_pack_mask_occupancy for
+ * the same mask: the head-dim-64 kernel takes its live key tiles from the
+ * map instead of scanning the packed rows; results are identical to
+ * sma_attn_fwd.  (Head dim 128 stages the packed rows anyway and ignores it.)
+ * No reference counterpart.
+ */
+SMA_API int sma_attn_fwd_occupancy(int dtype, const void* q, const void* k, const void* v, const void* mask_packed,
+                                   const void* occupancy, void* out, float* lse, int64_t B, int64_t H, int64_t N,
+                                   int64_t D, float scale, void* stream);
+
+/*
  * Synchronise `stream`, then report whether any kernel of this library on the
  * current device gave up a bounded device-side wait since the last clear
  * (SMA_ERR_TIMEOUT), or whether the stream holds a CUDA error (SMA_ERR_CUDA).

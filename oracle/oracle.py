@@ -12,6 +12,8 @@ here against them (pack_mask bit-exact, attention and LSE to FP32 rounding).
 
 Functions
   pack_mask(mask)                 python/sparse_attention.py:189-206
+  occupancy(mask)                 live (query tile, key tile) blocks of the mask,
+                                  the map the fused packer writes
                                   (same bits as csrc/sparse_attention.cu:20-42)
   attention(q, k, v, mask, scale) python/sparse_attention.py:26-44
   lse(q, k, mask, scale)          python/sparse_attention.py:74-76, with the
@@ -46,6 +48,26 @@ def pack_mask(mask):
     words = by.astype(np.uint32)
     packed = words[..., 0] | (words[..., 1] << 8) | (words[..., 2] << 16) | (words[..., 3] << 24)
     return packed.astype(np.uint32).view(np.int32)
+
+
+def occupancy(mask, tile=128):
+    """bool [B, H, N, N] -> int32 [B, H, ceil(N/tile), 2]: bit t of the pair
+    for query tile qt is set iff mask[..., tile*qt : tile*(qt+1), tile*t :
+    tile*(t+1)] has a True (t < 64).  The reference has no such map; this
+    restates what the fused packer must produce from the same mask, i.e.
+    which (query tile, key tile) blocks the reference's kernel would find
+    any kept key in (csrc/sparse_attention.cu:110-111 tests every bit)."""
+    mask = np.asarray(mask).astype(bool)
+    B, H, n, _ = mask.shape
+    qt = (n + tile - 1) // tile
+    pad = qt * tile - n
+    if pad:
+        mask = np.pad(mask, ((0, 0), (0, 0), (0, pad), (0, pad)))
+    blocks = mask.reshape(B, H, qt, tile, qt, tile).any(axis=(3, 5))  # [B, H, qt, kt]
+    out = np.zeros((B, H, qt, 2), dtype=np.uint32)
+    for t in range(min(qt, 64)):
+        out[..., t // 32] |= blocks[..., t].astype(np.uint32) << np.uint32(t % 32)
+    return out.view(np.int32)
 
 
 def unpack_mask(packed, n):

@@ -26,7 +26,8 @@
 //   0-3  softmax chain 0     4-7  softmax chain 1   (thread t of a warpgroup owns query row t)
 //        besides the softmax, each warpgroup scans the packed-mask rows of
 //        the item two ahead for live key tiles during its epilogue and
-//        publishes the list
+//        publishes the list (or, given the packer's occupancy map, reads the
+//        item's two words of live-tile bits from it instead)
 //   8    loader chain 0      9    loader chain 1
 //        TMA loads: Q (two buffers), K and V (two-stage rings), K one tile
 //        ahead of V so that a K copy never queues behind a V slot
@@ -211,7 +212,8 @@ template <bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_chain_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                          const uint32_t* __restrict__ mask, float* __restrict__ lse, int N, int BH, int W,
+                          const uint32_t* __restrict__ mask, const uint32_t* __restrict__ occ,
+                          float* __restrict__ lse, int N, int BH, int W,
                           int KT, int total_items, int vec, float scale_log2, uint32_t* err_word,
                           uint64_t timeout_ns) {
   extern __shared__ __align__(1024) uint8_t smem[];
@@ -547,8 +549,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         fail();
         return;
       }
-      const uint32_t lo = cc.part_lo[slot][0] | cc.part_lo[slot][1] | cc.part_lo[slot][2] | cc.part_lo[slot][3];
-      const uint32_t hi = cc.part_hi[slot][0] | cc.part_hi[slot][1] | cc.part_hi[slot][2] | cc.part_hi[slot][3];
+      uint32_t lo, hi;
+      if (occ != nullptr) {
+        // Live key tiles of the item straight from the packer's occupancy map.
+        const Item itj = item_of(chain_item(c, j), BH, QT, N);
+        const uint32_t* bits = occ + 2 * (static_cast<int64_t>(itj.bh) * QT + itj.q0 / kBM);
+        lo = bits[0];
+        hi = bits[1];
+      } else {
+        lo = cc.part_lo[slot][0] | cc.part_lo[slot][1] | cc.part_lo[slot][2] | cc.part_lo[slot][3];
+        hi = cc.part_hi[slot][0] | cc.part_hi[slot][1] | cc.part_hi[slot][2] | cc.part_hi[slot][3];
+      }
       uint32_t n = 0;
       for (int t = 0; t < KT; ++t) {
         const uint32_t bit = t < 32 ? (lo >> t) & 1u : (hi >> (t - 32)) & 1u;
@@ -560,7 +571,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     // Prologue: the live lists of the first two items.
     const int n_pre = n_items < 2 ? n_items : 2;
-    for (int j = 0; j < n_pre; ++j) {
+    for (int j = 0; occ == nullptr && j < n_pre; ++j) {
       uint32_t lo = 0u, hi = 0u;
       scan_rest(item_of(chain_item(c, j), BH, QT, N), 0, lo, hi);
       post_part(j, lo, hi);
@@ -695,7 +706,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // registers).
       const bool do_scan = i + 2 < n_items;
       const Item itn = item_of(chain_item(c, do_scan ? i + 2 : i), BH, QT, N);
-      if (do_scan && r < itn.rows_valid) {
+      if (do_scan && occ == nullptr && r < itn.rows_valid) {
         const uintptr_t a0 = reinterpret_cast<uintptr_t>(row_ptr(itn));
         const uintptr_t a1 = a0 + static_cast<uintptr_t>(W) * 4u;
         for (uintptr_t a = a0 & ~static_cast<uintptr_t>(127); a < a1; a += 128)
@@ -719,7 +730,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int e = 0; e < 32; ++e) h[e] = 0u;
       }
-      if (do_scan) {
+      if (do_scan && occ == nullptr) {
         uint32_t lo = 0u, hi = 0u;
         scan_rest(itn, 0, lo, hi);
         post_part(i + 2, lo, hi);
@@ -825,7 +836,7 @@ int launch(const AttnParams& p, const char** msg) {
   }
   const int vec = (W % 4 == 0 && (reinterpret_cast<uintptr_t>(p.mask) & 15u) == 0) ? 1 : 0;
   const int grid = static_cast<int>(total < sms[dev] ? total : sms[dev]);
-  kern<<<grid, kThreads, kSmemBytes, p.stream>>>(mq, mk, mv, mo, p.mask, p.lse, static_cast<int>(N),
+  kern<<<grid, kThreads, kSmemBytes, p.stream>>>(mq, mk, mv, mo, p.mask, p.occ, p.lse, static_cast<int>(N),
                                                  static_cast<int>(BH), static_cast<int>(W), static_cast<int>(KT),
                                                  static_cast<int>(total), vec, p.scale * kLog2e, p.err_word,
                                                  p.timeout_ns);

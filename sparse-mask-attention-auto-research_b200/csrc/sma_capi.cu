@@ -64,8 +64,13 @@ int sma_pack_mask(const void* mask, void* packed, int64_t B, int64_t H, int64_t 
   return rc == sma::kOk ? rc : fail(rc, msg);
 }
 
-int sma_attn_fwd(int dtype, const void* q, const void* k, const void* v, const void* mask_packed, void* out,
-                 float* lse, int64_t B, int64_t H, int64_t N, int64_t D, float scale, void* stream) {
+}  // extern "C"
+
+namespace {
+
+int attn_fwd_impl(int dtype, const void* q, const void* k, const void* v, const void* mask_packed,
+                  const uint32_t* occupancy, void* out, float* lse, int64_t B, int64_t H, int64_t N, int64_t D,
+                  float scale, void* stream) {
   if (dtype != SMA_DTYPE_FP16 && dtype != SMA_DTYPE_BF16)
     return fail(sma::kErrDtype, "attention: unsupported dtype, need fp16 or bf16");
   if (B < 0 || H < 0 || N < 0 || D <= 0) return fail(sma::kErrArg, "attention: bad dimension");
@@ -88,6 +93,7 @@ int sma_attn_fwd(int dtype, const void* q, const void* k, const void* v, const v
   p.k = k;
   p.v = v;
   p.mask = static_cast<const uint32_t*>(mask_packed);
+  p.occ = occupancy;
   p.out = out;
   p.lse = lse;
   p.B = B;
@@ -101,6 +107,36 @@ int sma_attn_fwd(int dtype, const void* q, const void* k, const void* v, const v
   const char* msg = nullptr;
   rc = sma::launch_attn_fwd(p, &msg);
   return rc == sma::kOk ? rc : fail(rc, msg);
+}
+
+}  // namespace
+
+extern "C" {
+
+int sma_attn_fwd(int dtype, const void* q, const void* k, const void* v, const void* mask_packed, void* out,
+                 float* lse, int64_t B, int64_t H, int64_t N, int64_t D, float scale, void* stream) {
+  return attn_fwd_impl(dtype, q, k, v, mask_packed, nullptr, out, lse, B, H, N, D, scale, stream);
+}
+
+int sma_pack_mask_occupancy(const void* mask, void* packed, void* occupancy, int64_t B, int64_t H, int64_t N,
+                            void* stream) {
+  if (B < 0 || H < 0 || N < 0) return fail(sma::kErrArg, "pack_mask_occupancy: negative dimension");
+  if (B == 0 || H == 0 || N == 0) return sma::kOk;
+  const char* msg = nullptr;
+  int rc = sma::launch_pack_mask_occ(static_cast<const uint8_t*>(mask), static_cast<uint32_t*>(packed),
+                                     static_cast<uint32_t*>(occupancy), B * H, N,
+                                     static_cast<cudaStream_t>(stream), &msg);
+  return rc == sma::kOk ? rc : fail(rc, msg);
+}
+
+int sma_attn_fwd_occupancy(int dtype, const void* q, const void* k, const void* v, const void* mask_packed,
+                           const void* occupancy, void* out, float* lse, int64_t B, int64_t H, int64_t N,
+                           int64_t D, float scale, void* stream) {
+  if (occupancy == nullptr) return fail(sma::kErrArg, "attention: null occupancy map");
+  if ((reinterpret_cast<uintptr_t>(occupancy) & 3u) != 0)
+    return fail(sma::kErrArg, "attention: occupancy map must be 4-byte aligned");
+  return attn_fwd_impl(dtype, q, k, v, mask_packed, static_cast<const uint32_t*>(occupancy), out, lse, B, H, N, D,
+                       scale, stream);
 }
 
 int sma_device_status(void* stream, int clear) {

@@ -29,6 +29,7 @@ struct AttnParams {
   float* lse;                 // [B, H, N] or nullptr
   int64_t B, H, N, D;
   float scale;
+  const uint32_t* occ;        // [B*H, ceil(N/128), 2] live key-tile bits per query tile, or nullptr
   uint32_t* err_word;         // device word the kernel ORs error bits into
   uint64_t timeout_ns;        // bound on every device-side wait
   cudaStream_t stream;
@@ -39,6 +40,12 @@ constexpr int64_t kMaxSeqLen = 8192;
 
 int launch_pack_mask(const uint8_t* mask, uint32_t* packed, int64_t rows, int64_t n,
                      cudaStream_t stream, const char** msg);
+
+// Packs like launch_pack_mask and writes the occupancy map `occ`
+// ([bh, ceil(n/128), 2] uint32: bit t = key tile t has a set bit in the
+// 128-row query tile).  Needs n % 32 == 0, n <= kMaxSeqLen, aligned pointers.
+int launch_pack_mask_occ(const uint8_t* mask, uint32_t* packed, uint32_t* occ, int64_t bh, int64_t n,
+                         cudaStream_t stream, const char** msg);
 
 int launch_attn_fwd(const AttnParams& p, const char** msg);
 

@@ -13,6 +13,11 @@ mask geometry), since the raw kernels would otherwise read out of bounds.
 ``lse`` may be None when ``is_training`` is False (the reference's
 ``sparse_attention_func`` passes None there and fails to bind it).
 
+Beyond the reference: ``pack_mask_occupancy(mask)`` packs and also returns
+the per-(batch*head, 128-row query tile) map of live 128-key tiles, and
+``forward(..., occupancy=map)`` lets the kernel skip dead tiles from that
+map instead of scanning the packed rows (same results).
+
 Work is enqueued on the current CUDA stream of the tensors' device,
 asynchronously, like the reference.
 """
@@ -33,8 +38,9 @@ def _require(cond, msg):
         raise RuntimeError(msg)
 
 
-def forward(q, k, v, mask_packed, out, lse, scale, is_training):
-    """Sparse attention forward (reference csrc/binding.cpp:9-47)."""
+def forward(q, k, v, mask_packed, out, lse, scale, is_training, occupancy=None):
+    """Sparse attention forward (reference csrc/binding.cpp:9-47).  The optional
+    ``occupancy`` is the map returned by pack_mask_occupancy for this mask."""
     _require(q.is_cuda, "q must be CUDA tensor")
     _require(q.dim() == 4, "q must be 4D")
     _require(q.dtype in _DTYPES, "Unsupported dtype, need BF16 or FP16")
@@ -62,6 +68,24 @@ def forward(q, k, v, mask_packed, out, lse, scale, is_training):
         _require(lse.is_contiguous(), "lse must be contiguous")
         lse_ptr = lse.data_ptr()
     lib = _lib.load()
+    if occupancy is not None:
+        q_tiles = (N + 127) // 128
+        _require(occupancy.device == q.device, "occupancy must be on the same device as q")
+        _require(occupancy.dtype in (torch.int32, torch.uint32), "occupancy must be int32/uint32")
+        _require(
+            tuple(occupancy.shape) == (B, H, q_tiles, 2),
+            f"occupancy must have shape {(B, H, q_tiles, 2)}, got {tuple(occupancy.shape)}",
+        )
+        _require(occupancy.is_contiguous(), "occupancy must be contiguous")
+        with torch.cuda.device(q.device):
+            _lib.check(
+                lib.sma_attn_fwd_occupancy(
+                    _DTYPES[q.dtype], q.data_ptr(), k.data_ptr(), v.data_ptr(), mask_packed.data_ptr(),
+                    occupancy.data_ptr(), out.data_ptr(), lse_ptr, B, H, N, D, float(scale),
+                    _stream_ptr(q.device),
+                )
+            )
+        return
     with torch.cuda.device(q.device):
         _lib.check(
             lib.sma_attn_fwd(
@@ -95,6 +119,38 @@ def pack_mask(mask):
     with torch.cuda.device(mask.device):
         _lib.check(lib.sma_pack_mask(mask.data_ptr(), packed.data_ptr(), B, H, N, _stream_ptr(mask.device)))
     return packed
+
+
+def occupancy_supported(mask):
+    """True when pack_mask_occupancy can handle this mask's geometry."""
+    N = mask.shape[-1]
+    return N % 32 == 0 and N <= _lib.SMA_MAX_SEQ_LEN and mask.data_ptr() % 16 == 0
+
+
+def pack_mask_occupancy(mask):
+    """bool [B, H, N, N] -> (int32 packed [B, H, N, ceil(N/32)], int32 occupancy
+    [B, H, ceil(N/128), 2] or None).  One pass over the mask; bit t of the
+    occupancy pair of query tile qt says whether key tile t has a set bit in
+    rows 128qt .. 128qt+127.  Shapes the fused packer does not take (N not a
+    multiple of 32, N above the maximum) fall back to pack_mask and None."""
+    _require(mask.is_cuda, "mask must be CUDA tensor")
+    _require(mask.dim() == 4, "mask must be 4D [B, H, N, N]")
+    _require(mask.dtype == torch.bool, "mask must be a bool tensor")
+    B, H, N, N2 = mask.shape
+    _require(N == N2, f"mask must be square in its last two dims, got {tuple(mask.shape)}")
+    mask = mask.contiguous()
+    if not occupancy_supported(mask):
+        return pack_mask(mask), None
+    packed = torch.empty((B, H, N, (N + 31) // 32), dtype=torch.int32, device=mask.device)
+    occupancy = torch.empty((B, H, (N + 127) // 128, 2), dtype=torch.int32, device=mask.device)
+    lib = _lib.load()
+    with torch.cuda.device(mask.device):
+        _lib.check(
+            lib.sma_pack_mask_occupancy(
+                mask.data_ptr(), packed.data_ptr(), occupancy.data_ptr(), B, H, N, _stream_ptr(mask.device)
+            )
+        )
+    return packed, occupancy
 
 
 def device_status(clear=True, device=None):

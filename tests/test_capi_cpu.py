@@ -75,6 +75,20 @@ def test_attn_rejects_bad_scale(lib):
         assert b"scale" in lib.sma_last_error()
 
 
+def test_fused_pack_rejects_unsupported(lib):
+    assert lib.sma_pack_mask_occupancy(16, 16, 16, 1, 1, 100, None) == L.SMA_ERR_ARG  # N % 32 != 0
+    assert lib.sma_pack_mask_occupancy(16, 16, 16, 1, 1, L.SMA_MAX_SEQ_LEN + 32, None) == L.SMA_ERR_UNSUPPORTED_N
+    assert lib.sma_pack_mask_occupancy(None, 16, 16, 1, 1, 64, None) == L.SMA_ERR_ARG
+    assert lib.sma_pack_mask_occupancy(8, 16, 16, 1, 1, 64, None) == L.SMA_ERR_ARG  # mask not 16-byte aligned
+    assert lib.sma_pack_mask_occupancy(None, None, None, 0, 4, 64, None) == L.SMA_OK
+
+
+def test_attn_with_map_rejects_bad_map(lib):
+    args = (0, 16, 16, 16, 16)
+    assert lib.sma_attn_fwd_occupancy(*args, None, 16, None, 1, 1, 64, 64, 0.125, None) == L.SMA_ERR_ARG
+    assert lib.sma_attn_fwd_occupancy(*args, 18, 16, None, 1, 1, 64, 64, 0.125, None) == L.SMA_ERR_ARG
+
+
 def test_empty_problems_are_noops(lib):
     assert _attn(lib, B=0) == L.SMA_OK
     assert lib.sma_pack_mask(None, None, 0, 4, 64, None) == L.SMA_OK

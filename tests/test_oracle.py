@@ -75,3 +75,21 @@ def test_planted_error_is_caught():
     assert np.abs(out - case["out"].numpy()).max() > 1e-3
     packed = oracle.pack_mask(m)
     assert not np.array_equal(packed, case["packed"].numpy())
+
+
+@pytest.mark.parametrize("path", golden_paths("pack") + golden_paths("attn"), ids=golden_ids("pack") + golden_ids("attn"))
+def test_occupancy_matches_reference_packed_bits(path):
+    """The occupancy restatement agrees with the reference's packed words:
+    a (query tile, key tile) block is live iff one of its packed words is
+    non-zero."""
+    case = load_golden(path)
+    mask = case["mask"].numpy()
+    n = mask.shape[-1]
+    words = case["packed"].numpy().view(np.uint32)  # reference bits [B, H, N, W]
+    occ = oracle.occupancy(mask).view(np.uint32)
+    qt = (n + 127) // 128
+    for t in range(min(qt, 64)):
+        cols = words[..., 4 * t:4 * t + 4]
+        for r in range(qt):
+            live = (cols[:, :, 128 * r:128 * (r + 1)] != 0).any(axis=(2, 3))
+            assert np.array_equal((occ[:, :, r, t // 32] >> (t % 32)) & 1, live.astype(np.uint32))
