@@ -29,14 +29,18 @@ extern "C" {
 #define SMA_ERR_UNSUPPORTED_D 3   /* head dim other than 64 or 128                  */
 #define SMA_ERR_LAUNCH 4          /* kernel launch failed                           */
 #define SMA_ERR_TIMEOUT 5         /* a device-side wait gave up (see sma_device_status) */
-#define SMA_ERR_UNSUPPORTED_N 6   /* sequence length above SMA_MAX_SEQ_LEN          */
+#define SMA_ERR_UNSUPPORTED_N 6   /* sequence length above the path's maximum       */
 #define SMA_ERR_CUDA 7            /* CUDA runtime / driver error                    */
 
 /* Element types of q, k, v and out. */
 #define SMA_DTYPE_FP16 0
 #define SMA_DTYPE_BF16 1
 
-#define SMA_MAX_SEQ_LEN 8192
+/* Longest supported sequence: 16384 at head dim 64, 8192 at head dim 128;
+ * the occupancy map (sma_pack_mask_occupancy) covers N <= 8192. */
+#define SMA_MAX_SEQ_LEN 16384
+#define SMA_MAX_SEQ_LEN_D128 8192
+#define SMA_MAX_SEQ_LEN_OCCUPANCY 8192
 
 #if defined(__GNUC__)
 #define SMA_API __attribute__((visibility("default")))
@@ -66,7 +70,8 @@ SMA_API int sma_pack_mask(const void* mask, void* packed, int64_t B, int64_t H, 
  * the scaled scores, or NULL to skip it (the reference's is_training=false).
  * Rows with no set bit get out = 0 and lse = -FLT_MAX (the reference CUDA
  * convention, csrc/sparse_attention.cu:133,141).
- * Supported: D in {64, 128}, 1 <= N <= SMA_MAX_SEQ_LEN, 16-byte aligned
+ * Supported: D in {64, 128}, 1 <= N <= SMA_MAX_SEQ_LEN (D = 64) or
+ * SMA_MAX_SEQ_LEN_D128 (D = 128), 16-byte aligned
  * q/k/v/out, scale finite and > 0 (the kernels fold the scale into the
  * exponent after the masked row max; the reference always passes 1/sqrt(D)).
  *
@@ -83,7 +88,7 @@ SMA_API int sma_attn_fwd(int dtype, const void* q, const void* k, const void* v,
  * sma_pack_mask does and `occupancy`: uint32 [B*H, ceil(N/128), 2], where bit t
  * of the pair for (batch*head, query tile qt) is set iff key tile t (keys
  * 128t .. 128t+127) has a set mask bit in query rows 128qt .. 128qt+127.
- * Needs N % 32 == 0, N <= SMA_MAX_SEQ_LEN, a 16-byte aligned mask and 4-byte
+ * Needs N % 32 == 0, N <= SMA_MAX_SEQ_LEN_OCCUPANCY, a 16-byte aligned mask and 4-byte
  * aligned outputs (SMA_ERR_ARG / SMA_ERR_UNSUPPORTED_N otherwise; callers
  * then use sma_pack_mask).  The packer reads every mask byte anyway, so the
  * map costs no extra HBM pass.

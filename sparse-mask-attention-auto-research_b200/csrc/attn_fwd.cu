@@ -693,8 +693,12 @@ __global__ void wait_probe_kernel(uint32_t* err_word, uint64_t timeout_ns) {
 }  // namespace
 
 int launch_attn_fwd(const AttnParams& p, const char** msg) {
-  if (p.N > kMaxSeqLen) {
-    *msg = "attention: sequence length above the supported maximum (8192)";
+  if (p.N > kMaxSeqLen || (p.D == 128 && p.N > kMaxSeqLenD128)) {
+    *msg = "attention: sequence length above the supported maximum (16384 for head dim 64, 8192 for 128)";
+    return kErrUnsupportedN;
+  }
+  if (p.occ != nullptr && p.N > kMaxSeqLenOcc) {
+    *msg = "attention: occupancy map given for a sequence length above 8192";
     return kErrUnsupportedN;
   }
   const bool bf = p.dtype == 1;

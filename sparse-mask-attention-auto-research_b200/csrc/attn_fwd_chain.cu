@@ -56,7 +56,8 @@ constexpr int kBM = 128;
 constexpr int kBN = 128;
 constexpr int kThreads = 384;
 constexpr int kSlots = 4;          // live-list slots per chain
-constexpr int kMaxTiles = 64;      // N <= 8192
+constexpr int kMaxTiles = 128;     // N <= 16384
+constexpr int kLiveWords = kMaxTiles / 32;  // live-tile bit words per item
 constexpr int kStages = 2;         // K ring and V ring depth per chain
 constexpr int kTileBytes = kBM * kD * 2;            // 16 KiB (Q, K, V or O tile)
 constexpr int kChainBytes = (2 + 2 * kStages + 1) * kTileBytes;
@@ -85,8 +86,7 @@ struct ChainCtl {
   uint64_t p_full;
   uint64_t pv_done;
   uint64_t drain;
-  uint32_t part_lo[kSlots][4];   // per-warp live-tile bits of the item being scanned
-  uint32_t part_hi[kSlots][4];
+  uint32_t part[kSlots][4][kLiveWords];  // per-warp live-tile bits of the item being scanned
   uint32_t n_live[kSlots];
   uint16_t live[kSlots][kMaxTiles];
 };
@@ -187,10 +187,16 @@ __device__ __forceinline__ void load_tile_words(const uint32_t* mrow, int kt, in
   }
 }
 
-__device__ __forceinline__ void set_live(int g, uint32_t x, uint32_t& lo, uint32_t& hi) {
+// Live-tile bits of one item (bit t = key tile t), kept in registers.
+struct LiveBits {
+  uint32_t w[kLiveWords];
+};
+
+__device__ __forceinline__ void set_live(int g, uint32_t x, LiveBits& b) {
   if (x != 0u) {
-    if (g < 32) lo |= 1u << g;
-    else hi |= 1u << (g - 32);
+    const uint32_t m = 1u << (g & 31);
+#pragma unroll
+    for (int k = 0; k < kLiveWords; ++k) b.w[k] |= (g >> 5) == k ? m : 0u;  // no dynamic register index
   }
 }
 
@@ -516,7 +522,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     // Live-tile bits of this thread's row of item j, from the 16-byte groups
     // at index >= g0 (groups below g0 were OR-ed by the caller).
-    auto scan_rest = [&](const Item& it, int g0, uint32_t& lo, uint32_t& hi) {
+    auto scan_rest = [&](const Item& it, int g0, LiveBits& bits) {
       if (r >= it.rows_valid) return;
       const uint32_t* mrow = row_ptr(it);
       if (vec) {
@@ -526,19 +532,18 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int u = 0; u < kScanBatch; ++u)
             v[u] = (gb + u < G4) ? __ldg(reinterpret_cast<const uint4*>(mrow) + gb + u) : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-          for (int u = 0; u < kScanBatch; ++u) set_live(gb + u, group_or(v[u], gb + u, N), lo, hi);
+          for (int u = 0; u < kScanBatch; ++u) set_live(gb + u, group_or(v[u], gb + u, N), bits);
         }
       } else {
-        for (int cw = g0 * 4; cw < W; ++cw) set_live(cw >> 2, __ldg(mrow + cw) & valid_bits(cw, N), lo, hi);
+        for (int cw = g0 * 4; cw < W; ++cw) set_live(cw >> 2, __ldg(mrow + cw) & valid_bits(cw, N), bits);
       }
     };
     // Stores this warp's share of item j's live bits (before a WG barrier).
-    auto post_part = [&](int j, uint32_t lo, uint32_t hi) {
-      lo = __reduce_or_sync(0xffffffffu, lo);
-      hi = __reduce_or_sync(0xffffffffu, hi);
-      if (lane == 0) {
-        cc.part_lo[j % kSlots][wq] = lo;
-        cc.part_hi[j % kSlots][wq] = hi;
+    auto post_part = [&](int j, const LiveBits& bits) {
+#pragma unroll
+      for (int k = 0; k < kLiveWords; ++k) {
+        const uint32_t x = __reduce_or_sync(0xffffffffu, bits.w[k]);
+        if (lane == 0) cc.part[j % kSlots][wq][k] = x;
       }
     };
     // Thread 0 of the WG, after a WG barrier: builds item j's live list and publishes it.
@@ -549,21 +554,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         fail();
         return;
       }
-      uint32_t lo, hi;
+      // Live key tiles straight from the packer's occupancy map when there is
+      // one (two words per item: the map is only made for N <= 8192).
+      const uint32_t* occ_j = nullptr;
       if (occ != nullptr) {
-        // Live key tiles of the item straight from the packer's occupancy map.
         const Item itj = item_of(chain_item(c, j), BH, QT, N);
-        const uint32_t* bits = occ + 2 * (static_cast<int64_t>(itj.bh) * QT + itj.q0 / kBM);
-        lo = bits[0];
-        hi = bits[1];
-      } else {
-        lo = cc.part_lo[slot][0] | cc.part_lo[slot][1] | cc.part_lo[slot][2] | cc.part_lo[slot][3];
-        hi = cc.part_hi[slot][0] | cc.part_hi[slot][1] | cc.part_hi[slot][2] | cc.part_hi[slot][3];
+        occ_j = occ + 2 * (static_cast<int64_t>(itj.bh) * QT + itj.q0 / kBM);
       }
       uint32_t n = 0;
-      for (int t = 0; t < KT; ++t) {
-        const uint32_t bit = t < 32 ? (lo >> t) & 1u : (hi >> (t - 32)) & 1u;
-        if (bit) cc.live[slot][n++] = static_cast<uint16_t>(t);
+      for (int k = 0; k * 32 < KT; ++k) {
+        uint32_t x;
+        if (occ_j != nullptr) {
+          x = k < 2 ? occ_j[k] : 0u;
+        } else {
+          x = cc.part[slot][0][k] | cc.part[slot][1][k] | cc.part[slot][2][k] | cc.part[slot][3][k];
+        }
+        while (x != 0u) {  // set bits in increasing key-tile order
+          const int b = __ffs(x) - 1;
+          x &= x - 1u;
+          if (k * 32 + b < KT) cc.live[slot][n++] = static_cast<uint16_t>(k * 32 + b);
+        }
       }
       cc.n_live[slot] = n;
       mbar_arrive(smem_u32(&cc.sched_full[slot]));
@@ -572,9 +582,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Prologue: the live lists of the first two items.
     const int n_pre = n_items < 2 ? n_items : 2;
     for (int j = 0; occ == nullptr && j < n_pre; ++j) {
-      uint32_t lo = 0u, hi = 0u;
-      scan_rest(item_of(chain_item(c, j), BH, QT, N), 0, lo, hi);
-      post_part(j, lo, hi);
+      LiveBits bits{};
+      scan_rest(item_of(chain_item(c, j), BH, QT, N), 0, bits);
+      post_part(j, bits);
     }
     named_bar_sync(bar_id, 128);
     if (r == 0)
@@ -731,9 +741,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int e = 0; e < 32; ++e) h[e] = 0u;
       }
       if (do_scan && occ == nullptr) {
-        uint32_t lo = 0u, hi = 0u;
-        scan_rest(itn, 0, lo, hi);
-        post_part(i + 2, lo, hi);
+        LiveBits bits{};
+        scan_rest(itn, 0, bits);
+        post_part(i + 2, bits);
       }
       // The previous item's O store must have finished reading the staging tile.
       if (r == 0) bulk_wait_group_read0();

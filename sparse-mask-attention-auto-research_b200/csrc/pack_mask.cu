@@ -194,8 +194,8 @@ int launch_pack_mask_occ(const uint8_t* mask, uint32_t* packed, uint32_t* occ, i
     *msg = "pack_mask_occupancy: needs N % 32 == 0, a 16-byte aligned mask and 4-byte aligned outputs";
     return kErrArg;
   }
-  if (n > kMaxSeqLen) {
-    *msg = "pack_mask_occupancy: sequence length above the supported maximum (8192)";
+  if (n > kMaxSeqLenOcc) {
+    *msg = "pack_mask_occupancy: sequence length above the occupancy map's maximum (8192)";
     return kErrUnsupportedN;
   }
   const int64_t q_tiles = (n + kOccTileRows - 1) / kOccTileRows;

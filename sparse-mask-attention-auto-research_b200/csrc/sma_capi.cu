@@ -75,8 +75,11 @@ int attn_fwd_impl(int dtype, const void* q, const void* k, const void* v, const 
     return fail(sma::kErrDtype, "attention: unsupported dtype, need fp16 or bf16");
   if (B < 0 || H < 0 || N < 0 || D <= 0) return fail(sma::kErrArg, "attention: bad dimension");
   if (D != 64 && D != 128) return fail(sma::kErrUnsupportedD, "attention: head dim must be 64 or 128");
-  if (N > SMA_MAX_SEQ_LEN)
-    return fail(sma::kErrUnsupportedN, "attention: sequence length above the supported maximum (8192)");
+  if (N > SMA_MAX_SEQ_LEN || (D == 128 && N > SMA_MAX_SEQ_LEN_D128))
+    return fail(sma::kErrUnsupportedN,
+                "attention: sequence length above the supported maximum (16384 for head dim 64, 8192 for 128)");
+  if (occupancy != nullptr && N > SMA_MAX_SEQ_LEN_OCCUPANCY)
+    return fail(sma::kErrUnsupportedN, "attention: occupancy map given for a sequence length above 8192");
   if (!(scale > 0.f) || !(scale < INFINITY)) return fail(sma::kErrArg, "attention: scale must be finite and > 0");
   if (B == 0 || H == 0 || N == 0) return sma::kOk;
   if (!q || !k || !v || !mask_packed || !out) return fail(sma::kErrArg, "attention: null pointer");
@@ -121,6 +124,8 @@ int sma_attn_fwd(int dtype, const void* q, const void* k, const void* v, const v
 int sma_pack_mask_occupancy(const void* mask, void* packed, void* occupancy, int64_t B, int64_t H, int64_t N,
                             void* stream) {
   if (B < 0 || H < 0 || N < 0) return fail(sma::kErrArg, "pack_mask_occupancy: negative dimension");
+  if (N > SMA_MAX_SEQ_LEN_OCCUPANCY)
+    return fail(sma::kErrUnsupportedN, "pack_mask_occupancy: sequence length above the occupancy map's maximum (8192)");
   if (B == 0 || H == 0 || N == 0) return sma::kOk;
   const char* msg = nullptr;
   int rc = sma::launch_pack_mask_occ(static_cast<const uint8_t*>(mask), static_cast<uint32_t*>(packed),

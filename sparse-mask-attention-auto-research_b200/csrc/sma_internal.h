@@ -35,15 +35,20 @@ struct AttnParams {
   cudaStream_t stream;
 };
 
-// Largest sequence length the fused kernel stages a full mask row-block for.
-constexpr int64_t kMaxSeqLen = 8192;
+// Largest sequence length per path: the head-dim-64 kernel keeps a live-tile
+// list of up to 128 key tiles per query tile; the head-dim-128 kernel stages a
+// 64-row block of packed mask words (N/32 words a row) in shared memory; the
+// occupancy map holds two 32-bit words (64 key tiles) per query tile.
+constexpr int64_t kMaxSeqLen = 16384;
+constexpr int64_t kMaxSeqLenD128 = 8192;
+constexpr int64_t kMaxSeqLenOcc = 8192;
 
 int launch_pack_mask(const uint8_t* mask, uint32_t* packed, int64_t rows, int64_t n,
                      cudaStream_t stream, const char** msg);
 
 // Packs like launch_pack_mask and writes the occupancy map `occ`
 // ([bh, ceil(n/128), 2] uint32: bit t = key tile t has a set bit in the
-// 128-row query tile).  Needs n % 32 == 0, n <= kMaxSeqLen, aligned pointers.
+// 128-row query tile).  Needs n % 32 == 0, n <= kMaxSeqLenOcc, aligned pointers.
 int launch_pack_mask_occ(const uint8_t* mask, uint32_t* packed, uint32_t* occ, int64_t bh, int64_t n,
                          cudaStream_t stream, const char** msg);
 

@@ -124,7 +124,7 @@ def pack_mask(mask):
 def occupancy_supported(mask):
     """True when pack_mask_occupancy can handle this mask's geometry."""
     N = mask.shape[-1]
-    return N % 32 == 0 and N <= _lib.SMA_MAX_SEQ_LEN and mask.data_ptr() % 16 == 0
+    return N % 32 == 0 and N <= _lib.SMA_MAX_SEQ_LEN_OCCUPANCY and mask.data_ptr() % 16 == 0
 
 
 def pack_mask_occupancy(mask):

@@ -60,6 +60,11 @@ def test_attn_rejects_head_dim(lib):
 
 def test_attn_rejects_long_sequence(lib):
     assert _attn(lib, N=L.SMA_MAX_SEQ_LEN + 1) == L.SMA_ERR_UNSUPPORTED_N
+    assert _attn(lib, N=L.SMA_MAX_SEQ_LEN_D128 + 1, D=128) == L.SMA_ERR_UNSUPPORTED_N
+    assert b"16384" in lib.sma_last_error()
+    # The map holds 64 key tiles per query tile: longer sequences are refused with it.
+    args = (0, 16, 16, 16, 16, 16, 16, None, 1, 1, L.SMA_MAX_SEQ_LEN_OCCUPANCY + 1, 64, 0.125, None)
+    assert lib.sma_attn_fwd_occupancy(*args) == L.SMA_ERR_UNSUPPORTED_N
 
 
 def test_attn_rejects_bad_args(lib):
@@ -77,7 +82,7 @@ def test_attn_rejects_bad_scale(lib):
 
 def test_fused_pack_rejects_unsupported(lib):
     assert lib.sma_pack_mask_occupancy(16, 16, 16, 1, 1, 100, None) == L.SMA_ERR_ARG  # N % 32 != 0
-    assert lib.sma_pack_mask_occupancy(16, 16, 16, 1, 1, L.SMA_MAX_SEQ_LEN + 32, None) == L.SMA_ERR_UNSUPPORTED_N
+    assert lib.sma_pack_mask_occupancy(16, 16, 16, 1, 1, L.SMA_MAX_SEQ_LEN_OCCUPANCY + 32, None) == L.SMA_ERR_UNSUPPORTED_N
     assert lib.sma_pack_mask_occupancy(None, 16, 16, 1, 1, 64, None) == L.SMA_ERR_ARG
     assert lib.sma_pack_mask_occupancy(8, 16, 16, 1, 1, 64, None) == L.SMA_ERR_ARG  # mask not 16-byte aligned
     assert lib.sma_pack_mask_occupancy(None, None, None, 0, 4, 64, None) == L.SMA_OK
