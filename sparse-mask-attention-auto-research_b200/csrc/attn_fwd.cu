@@ -193,6 +193,8 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctl.tmem_base;
+  // Set-up above overlaps the previous kernel in the stream (see launch_pdl).
+  pdl_wait_prior_grid();
 
   if (warp == 4) {
     // ------------------------------------------------------------ producer
@@ -664,10 +666,10 @@ int launch_impl(const AttnParams& p, const char** msg) {
     smem_set[dev] = smem;
   }
   const float scale_log2 = p.scale * kLog2e;
-  kern<<<static_cast<unsigned>(QT * BH), kThreads, smem, p.stream>>>(
-      mq, mk, mv, mo, p.mask, p.lse, static_cast<int>(N), static_cast<int>(BH), static_cast<int>(W),
-      static_cast<int>(KT), scale_log2, p.err_word, p.timeout_ns);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(kern, static_cast<unsigned>(QT * BH), kThreads, smem, p.stream, mq, mk, mv, mo, p.mask,
+                             p.lse, static_cast<int>(N), static_cast<int>(BH), static_cast<int>(W),
+                             static_cast<int>(KT), scale_log2, p.err_word, p.timeout_ns);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     *msg = cudaGetErrorString(e);
     return kErrLaunch;

@@ -286,6 +286,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = ctl.tmem_base;
+  // Set-up above overlaps the previous kernel (the mask packer); its outputs
+  // and everything else earlier in the stream are read only after this.
+  pdl_wait_prior_grid();
 
   auto fail = [&]() {
     ctl.abort_flag = 1;
@@ -520,6 +523,14 @@ __global__ void __launch_bounds__(kThreads, 1)
         mw[0] = mw[1] = mw[2] = mw[3] = 0u;
       }
     };
+    // This thread's packed-mask row of `it` into L1 (a prefetch holds no registers).
+    auto prefetch_rows_l1 = [&](const Item& it) {
+      if (r >= it.rows_valid) return;
+      const uintptr_t a0 = reinterpret_cast<uintptr_t>(row_ptr(it));
+      const uintptr_t a1 = a0 + static_cast<uintptr_t>(W) * 4u;
+      for (uintptr_t a = a0 & ~static_cast<uintptr_t>(127); a < a1; a += 128)
+        asm volatile("prefetch.global.L1 [%0];" ::"l"(a));
+    };
     // Live-tile bits of this thread's row of item j, from the 16-byte groups
     // at index >= g0 (groups below g0 were OR-ed by the caller).
     auto scan_rest = [&](const Item& it, int g0, LiveBits& bits) {
@@ -579,16 +590,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_arrive(smem_u32(&cc.sched_full[slot]));
     };
 
-    // Prologue: the live lists of the first two items.
+    // Prologue: the live lists of the first two items.  The second item's
+    // mask rows are prefetched into L1 first, so both rows are fetched from
+    // HBM at once, and the first list is published before the second is built.
     const int n_pre = n_items < 2 ? n_items : 2;
-    for (int j = 0; occ == nullptr && j < n_pre; ++j) {
-      LiveBits bits{};
-      scan_rest(item_of(chain_item(c, j), BH, QT, N), 0, bits);
-      post_part(j, bits);
+    if (n_pre > 1 && occ == nullptr) prefetch_rows_l1(item_of(chain_item(c, 1), BH, QT, N));
+    for (int j = 0; j < n_pre; ++j) {
+      if (occ == nullptr) {
+        LiveBits bits{};
+        scan_rest(item_of(chain_item(c, j), BH, QT, N), 0, bits);
+        post_part(j, bits);
+      }
+      named_bar_sync(bar_id, 128);
+      if (r == 0) publish(j);
     }
-    named_bar_sync(bar_id, 128);
-    if (r == 0)
-      for (int j = 0; j < n_pre; ++j) publish(j);
 
     uint32_t mw[4] = {0u, 0u, 0u, 0u};
     bool have_mw = false;  // mw already holds tile 0 of the current item
@@ -716,12 +731,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // registers).
       const bool do_scan = i + 2 < n_items;
       const Item itn = item_of(chain_item(c, do_scan ? i + 2 : i), BH, QT, N);
-      if (do_scan && occ == nullptr && r < itn.rows_valid) {
-        const uintptr_t a0 = reinterpret_cast<uintptr_t>(row_ptr(itn));
-        const uintptr_t a1 = a0 + static_cast<uintptr_t>(W) * 4u;
-        for (uintptr_t a = a0 & ~static_cast<uintptr_t>(127); a < a1; a += 128)
-          asm volatile("prefetch.global.L1 [%0];" ::"l"(a));
-      }
+      if (do_scan && occ == nullptr) prefetch_rows_l1(itn);
       // O of the item, normalised and packed to 16-bit pairs (32 words per row).
       const float inv = (l_out > 0.f) ? (1.f / l_out) : 0.f;
       uint32_t h[32];
@@ -846,11 +856,11 @@ int launch(const AttnParams& p, const char** msg) {
   }
   const int vec = (W % 4 == 0 && (reinterpret_cast<uintptr_t>(p.mask) & 15u) == 0) ? 1 : 0;
   const int grid = static_cast<int>(total < sms[dev] ? total : sms[dev]);
-  kern<<<grid, kThreads, kSmemBytes, p.stream>>>(mq, mk, mv, mo, p.mask, p.occ, p.lse, static_cast<int>(N),
-                                                 static_cast<int>(BH), static_cast<int>(W), static_cast<int>(KT),
-                                                 static_cast<int>(total), vec, p.scale * kLog2e, p.err_word,
-                                                 p.timeout_ns);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e = launch_pdl(kern, static_cast<unsigned>(grid), kThreads, kSmemBytes, p.stream, mq, mk, mv, mo,
+                             p.mask, p.occ, p.lse, static_cast<int>(N), static_cast<int>(BH), static_cast<int>(W),
+                             static_cast<int>(KT), static_cast<int>(total), vec, p.scale * kLog2e, p.err_word,
+                             p.timeout_ns);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     static thread_local char buf[256];
     cudaFuncAttributes fa{};

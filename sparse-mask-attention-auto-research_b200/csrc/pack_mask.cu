@@ -17,6 +17,7 @@
 // General path: one thread per output word with byte loads (any N, any
 // alignment).
 #include "sma_internal.h"
+#include "sma_ptx.cuh"
 
 namespace sma {
 namespace {
@@ -39,6 +40,7 @@ constexpr int kOccTileRows = 128;  // query rows per occupancy item (the attenti
 
 __global__ void __launch_bounds__(kPackThreads) pack_mask_aligned_kernel(
     const uint4* __restrict__ in, uint32_t* __restrict__ out, int64_t total_words) {
+  pdl_launch_dependents();  // the attention kernel after this one may start its set-up
   const int lane = threadIdx.x & 31;
   const int64_t warp_global = (static_cast<int64_t>(blockIdx.x) * kPackThreads + threadIdx.x) >> 5;
   const int64_t base = warp_global * (32 * kPackRounds);
@@ -64,6 +66,7 @@ __global__ void __launch_bounds__(kPackThreads) pack_mask_aligned_kernel(
 __global__ void __launch_bounds__(kPackThreads) pack_mask_generic_kernel(
     const uint8_t* __restrict__ in, uint32_t* __restrict__ out, int64_t rows, int64_t n,
     int64_t n_words) {
+  pdl_launch_dependents();  // the attention kernel after this one may start its set-up
   const int64_t idx = static_cast<int64_t>(blockIdx.x) * kPackThreads + threadIdx.x;
   if (idx >= rows * n_words) return;
   const int64_t row = idx / n_words;
@@ -87,6 +90,7 @@ constexpr int kOccThreads = 256;  // one item (128 rows x N/32 words) per CTA
 __global__ void __launch_bounds__(kOccThreads) pack_mask_occ_kernel(
     const uint4* __restrict__ in, uint32_t* __restrict__ out, uint32_t* __restrict__ occ, int n, int n_words,
     int q_tiles) {
+  pdl_launch_dependents();  // the attention kernel after this one may start its set-up
   __shared__ uint32_t s_bits[2];
   const int item = blockIdx.x;  // batch*head * q_tiles + query tile
   const int bh = item / q_tiles;

@@ -54,6 +54,25 @@ int launch_pack_mask_occ(const uint8_t* mask, uint32_t* packed, uint32_t* occ, i
 
 int launch_attn_fwd(const AttnParams& p, const char** msg);
 
+// Launches `kern` with programmatic stream serialisation: its CTAs may start
+// (and run their set-up) while the previous kernel in the stream finishes;
+// the kernel itself calls griddepcontrol.wait before reading global memory.
+template <typename... Params, typename... Args>
+cudaError_t launch_pdl(void (*kern)(Params...), unsigned grid, unsigned block, size_t smem, cudaStream_t stream,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<Params>(args)...);
+}
+
 // Persistent two-chain kernel (attn_fwd_chain.cu): head dim 64, any
 // supported N.  launch_attn_fwd dispatches to it when chain_supported().
 bool chain_supported(const AttnParams& p);
