@@ -386,8 +386,8 @@ def run_ours(args):
         return 0
 
     peaks = load_peaks()
-    # D = 64: the persistent two-chain kernel; D = 128: the two-CTA-per-SM kernel.
-    attn_kernel = "attn_fwd_chain_kernel" if D == 64 else "attn_fwd_kernel"
+    # Both head dims run the persistent two-chain kernel.
+    attn_kernel = "attn_fwd_chain_kernel"
     bm, bn = workloads.kernel_tile(D)
     live = workloads.live_tile_fraction(m, bm, bn)
     a_bytes = workloads.attn_bytes(lb, lh, N, D)

@@ -1,9 +1,9 @@
-// Persistent two-chain fused masked-softmax attention forward, head dim 64
-// (sm_100a).
+// Persistent two-chain fused masked-softmax attention forward, head dims 64
+// and 128 (sm_100a).
 //
-// Same computation as attn_fwd.cu (reference csrc/sparse_attention.cu:64-143):
-// O = softmax_masked(scale * Q K^T) V per (batch*head, query row); rows with
-// no set mask bit give O = 0 and lse = -FLT_MAX.
+// O = softmax_masked(scale * Q K^T) V per (batch*head, query row), the
+// reference forward (csrc/sparse_attention.cu:64-143); rows with no set mask
+// bit give O = 0 and lse = -FLT_MAX.
 //
 // One CTA per SM runs two independent "chains".  A chain is one softmax
 // warpgroup plus its own loader warp and MMA warp; it walks its own list of
@@ -13,11 +13,12 @@
 // tensor-core result, a copy or its epilogue, the other keeps the
 // exponential unit busy.
 //
-// Per chain and live 128-key tile g (tiles with no set bit in the item's
-// rows are skipped before their K/V are loaded):
-//   MMA warp:  S = Q K_g^T            (4 x tcgen05.mma M=128 N=128 K=16)
+// Per chain and live key tile g (BN = 128 keys for D = 64, 64 keys for
+// D = 128; tiles with no set bit in the item's rows are skipped before their
+// K/V are loaded):
+//   MMA warp:  S = Q K_g^T            (D/16 x tcgen05.mma M=128 N=BN K=16)
 //   softmax:   read S, mask, row max, P = 2^(S*scale*log2e - m), write P (fp16/bf16)
-//   MMA warp:  O += P V_g             (8 x tcgen05.mma M=128 N=64 K=16, P from TMEM)
+//   MMA warp:  O += P V_g             (BN/16 x tcgen05.mma M=128 N=D K=16, P from TMEM)
 // S and P occupy separate TMEM columns: as soon as the softmax has copied S
 // into registers, the MMA warp issues Q K_{g+1}^T into the same columns, so
 // the next S is ready when the current exponentials are done.
@@ -27,17 +28,18 @@
 //        besides the softmax, each warpgroup scans the packed-mask rows of
 //        the item two ahead for live key tiles during its epilogue and
 //        publishes the list (or, given the packer's occupancy map, reads the
-//        item's two words of live-tile bits from it instead)
+//        item's two words of live-tile bits from it instead; D = 64 only)
 //   8    loader chain 0      9    loader chain 1
-//        TMA loads: Q (two buffers), K and V (two-stage rings), K one tile
-//        ahead of V so that a K copy never queues behind a V slot
+//        TMA loads: Q, K and V (two-stage rings), K one tile ahead of V so
+//        that a K copy never queues behind a V slot
 //   10   MMA chain 0 (+ TMEM allocation)   11  MMA chain 1
 //
-// TMEM (512 columns): chain c at 256c: S [0,128) | P [128,192) | O [192,256)
-// Shared memory: per chain Q[2] K[2] V[2] O-staging, 16 KiB each (224 KiB),
-// plus the control block.
-// The softmax reads its row's four mask words per tile with one 16-byte
-// global load issued a tile ahead.
+// TMEM (512 columns): chain c at 256c: S [0,BN) | P [BN,3BN/2) | O [3BN/2, 3BN/2+D)
+// Shared memory per chain: D = 64: Q[2] K[2] V[2] and an O staging tile,
+// 16 KiB each (O leaves by TMA store); D = 128: Q (32 KiB) K[2] V[2] (16
+// KiB each; O is stored from registers).  Plus the control block.
+// The softmax reads its row's mask words of the next tile with one 16- or
+// 8-byte global load issued a tile ahead.
 // Every wait is bounded (mbar_wait_bounded) and reports through err_word.
 #include <cfloat>
 #include <cstdio>
@@ -51,22 +53,39 @@
 namespace sma {
 namespace {
 
-constexpr int kD = 64;
 constexpr int kBM = 128;
-constexpr int kBN = 128;
 constexpr int kThreads = 384;
 constexpr int kSlots = 4;          // live-list slots per chain
-constexpr int kMaxTiles = 128;     // N <= 16384
+constexpr int kMaxTiles = 128;     // key tiles per item: N <= 16384 (D = 64), N <= 8192 (D = 128)
 constexpr int kLiveWords = kMaxTiles / 32;  // live-tile bit words per item
 constexpr int kStages = 2;         // K ring and V ring depth per chain
-constexpr int kTileBytes = kBM * kD * 2;            // 16 KiB (Q, K, V or O tile)
-constexpr int kChainBytes = (2 + 2 * kStages + 1) * kTileBytes;
 constexpr int kTmemCols = 512;
 constexpr int kChainCols = 256;
-constexpr int kSCol = 0;
-constexpr int kPCol = 128;
-constexpr int kOCol = 192;
 constexpr int kScanBatch = 4;      // 16-byte mask loads in flight per thread while scanning
+
+// Per head dim: D = 64 takes 128-key tiles, D = 128 takes 64-key tiles, so a
+// K or V tile is 16 KiB either way and S + P + O of a chain fit its 256 TMEM
+// columns.  Q (and O) rows are D / 64 swizzle chunks of 128 bytes.
+template <int D>
+struct ChainCfg {
+  static_assert(D == 64 || D == 128, "head dim");
+  static constexpr int kBN = D == 64 ? 128 : 64;       // keys per tile
+  static constexpr int kWords = kBN / 32;              // packed-mask words of a row per tile
+  static constexpr int kTilesPerGroup = 4 / kWords;    // tiles per 16-byte group of a mask row
+  static constexpr int kDChunks = D / 64;
+  static constexpr int kQBytes = kBM * D * 2;          // 16 / 32 KiB
+  static constexpr int kKVBytes = kBN * D * 2;         // 16 KiB
+  static constexpr int kQBufs = D == 64 ? 2 : 1;
+  // O leaves through a TMA store from a staging tile (D = 64) or straight
+  // from registers (D = 128, which has no shared memory left for staging).
+  static constexpr bool kStageO = D == 64;
+  static constexpr int kChainBytes = kQBufs * kQBytes + 2 * kStages * kKVBytes + (kStageO ? kQBytes : 0);
+  static constexpr int kSCol = 0;
+  static constexpr int kPCol = kBN;
+  static constexpr int kOCol = kBN + kBN / 2;
+  static_assert(kOCol + D <= kChainCols, "TMEM budget");
+  static constexpr int kMaxN = kMaxTiles * kBN;
+};
 constexpr float kRescaleThreshold = 8.0f;
 constexpr float kLn2 = 0.69314718055994530942f;
 constexpr float kLog2e = 1.44269504088896340736f;
@@ -75,7 +94,7 @@ constexpr int kMaxDevices = 64;
 struct ChainCtl {
   uint64_t sched_full[kSlots];
   uint64_t sched_empty[kSlots];  // 4 softmax warps + MMA warp + loader
-  uint64_t q_full[2];
+  uint64_t q_full[2];   // per Q buffer (one or two)
   uint64_t q_empty[2];
   uint64_t k_full[kStages];
   uint64_t k_empty[kStages];
@@ -97,8 +116,11 @@ struct Ctl {
   uint32_t abort_flag;
 };
 
-constexpr size_t kSmemBytes = 2 * static_cast<size_t>(kChainBytes) + sizeof(Ctl);
-static_assert(kSmemBytes <= 227 * 1024, "shared memory budget");
+template <int D>
+constexpr size_t smem_bytes() {
+  return 2 * static_cast<size_t>(ChainCfg<D>::kChainBytes) + sizeof(Ctl);
+}
+static_assert(smem_bytes<64>() <= 227 * 1024 && smem_bytes<128>() <= 227 * 1024, "shared memory budget");
 
 __device__ __forceinline__ float ex2f(float x) {
   float y;
@@ -168,22 +190,32 @@ __device__ __forceinline__ uint32_t valid_bits(int cw, int N) {
   return valid >= 32 ? 0xFFFFFFFFu : (valid <= 0 ? 0u : ((1u << valid) - 1u));
 }
 
-// The four mask words of key tile kt for one query row, columns >= N cleared.
+// The mask words of key tile kt (kWords of them) for one query row, columns
+// >= N cleared.
+template <int D>
 __device__ __forceinline__ void load_tile_words(const uint32_t* mrow, int kt, int W, int N, bool vec,
-                                                uint32_t (&mw)[4]) {
+                                                uint32_t (&mw)[ChainCfg<D>::kWords]) {
+  using C = ChainCfg<D>;
+  const int w0 = kt * C::kWords;
   if (vec) {
-    const uint4 v = __ldg(reinterpret_cast<const uint4*>(mrow + kt * 4));
-    mw[0] = v.x;
-    mw[1] = v.y;
-    mw[2] = v.z;
-    mw[3] = v.w;
+    if constexpr (C::kWords == 4) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(mrow + w0));
+      mw[0] = v.x;
+      mw[1] = v.y;
+      mw[2] = v.z;
+      mw[3] = v.w;
+    } else {
+      const uint2 v = __ldg(reinterpret_cast<const uint2*>(mrow + w0));
+      mw[0] = v.x;
+      mw[1] = v.y;
+    }
   } else {
 #pragma unroll
-    for (int w = 0; w < 4; ++w) mw[w] = (kt * 4 + w < W) ? __ldg(mrow + kt * 4 + w) : 0u;
+    for (int w = 0; w < C::kWords; ++w) mw[w] = (w0 + w < W) ? __ldg(mrow + w0 + w) : 0u;
   }
-  if (N - kt * kBN < kBN) {
+  if (N - kt * C::kBN < C::kBN) {
 #pragma unroll
-    for (int w = 0; w < 4; ++w) mw[w] &= valid_bits(kt * 4 + w, N);
+    for (int w = 0; w < C::kWords; ++w) mw[w] &= valid_bits(w0 + w, N);
   }
 }
 
@@ -200,11 +232,18 @@ __device__ __forceinline__ void set_live(int g, uint32_t x, LiveBits& b) {
   }
 }
 
-// OR of the four words of 16-byte group g (key tile g), columns >= N cleared.
-__device__ __forceinline__ uint32_t group_or(const uint4& v, int g, int N) {
-  if (N - g * kBN >= kBN) return v.x | v.y | v.z | v.w;
-  return (v.x & valid_bits(g * 4, N)) | (v.y & valid_bits(g * 4 + 1, N)) | (v.z & valid_bits(g * 4 + 2, N)) |
-         (v.w & valid_bits(g * 4 + 3, N));
+// Live bits of the key tiles in 16-byte group g of a mask row (words 4g ..
+// 4g+3: one 128-key tile, or two 64-key tiles), columns >= N cleared.
+template <int D>
+__device__ __forceinline__ void group_live(const uint4& v, int g, int N, LiveBits& bits) {
+  const uint32_t x0 = v.x & valid_bits(g * 4, N), x1 = v.y & valid_bits(g * 4 + 1, N);
+  const uint32_t x2 = v.z & valid_bits(g * 4 + 2, N), x3 = v.w & valid_bits(g * 4 + 3, N);
+  if constexpr (ChainCfg<D>::kWords == 4) {
+    set_live(g, x0 | x1 | x2 | x3, bits);
+  } else {
+    set_live(2 * g, x0 | x1, bits);
+    set_live(2 * g + 1, x2 | x3, bits);
+  }
 }
 
 // Position of one chain in the flattened sequence of its live tiles.
@@ -214,21 +253,25 @@ struct Cursor {
   uint32_t n;  // live tiles of item i
 };
 
-template <bool BF16>
+template <int D, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_chain_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
-                          const uint32_t* __restrict__ mask, const uint32_t* __restrict__ occ,
-                          float* __restrict__ lse, int N, int BH, int W,
+                          uint16_t* __restrict__ out, const uint32_t* __restrict__ mask,
+                          const uint32_t* __restrict__ occ, float* __restrict__ lse, int N, int BH, int W,
                           int KT, int total_items, int vec, float scale_log2, uint32_t* err_word,
                           uint64_t timeout_ns) {
+  using C = ChainCfg<D>;
+  constexpr int kBN = C::kBN;
+  constexpr int kWords = C::kWords;
+  constexpr int kSCol = C::kSCol, kPCol = C::kPCol, kOCol = C::kOCol;
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t base = smem_u32(smem);
   if ((base & 1023u) != 0u) {
     if (threadIdx.x == 0) atomicOr(err_word, kDevErrLayout);
     return;
   }
-  Ctl& ctl = *reinterpret_cast<Ctl*>(smem + 2 * kChainBytes);
+  Ctl& ctl = *reinterpret_cast<Ctl*>(smem + 2 * C::kChainBytes);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -326,27 +369,31 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int c = warp - 8;
     ChainCtl& cc = ctl.ch[c];
     if (lane == 0) {
-      const uint32_t sQ = base + c * kChainBytes;
-      const uint32_t sK = sQ + 2 * kTileBytes;
-      const uint32_t sV = sK + kStages * kTileBytes;
+      const uint32_t sQ = base + c * C::kChainBytes;
+      const uint32_t sK = sQ + C::kQBufs * C::kQBytes;
+      const uint32_t sV = sK + kStages * C::kKVBytes;
       const int n_items = chain_items(c);
       tma_prefetch_desc(&tm_q);
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
-      tma_prefetch_desc(&tm_o);
+      if constexpr (C::kStageO) tma_prefetch_desc(&tm_o);
       Cursor kc{-1, 0u, 0u}, vc{-1, 0u, 0u};
       uint32_t gk = 0, gv = 0, q_count = 0;  // K, V and Q copies issued
       bool ok = true;
       auto issue_k = [&]() -> bool {
         const Item it = item_of(chain_item(c, kc.i), BH, QT, N);
         if (kc.t == 0) {
-          // First tile of an item: its Q, into the buffer the item two back used.
-          const int qb = q_count & 1;
-          if (q_count >= 2 &&
-              !mbar_wait_bounded(smem_u32(&cc.q_empty[qb]), ((q_count - 2) >> 1) & 1, abort_flag, timeout_ns))
+          // First tile of an item: its Q, into the buffer the item kQBufs back used.
+          const int qb = q_count % C::kQBufs;
+          if (q_count >= static_cast<uint32_t>(C::kQBufs) &&
+              !mbar_wait_bounded(smem_u32(&cc.q_empty[qb]), ((q_count / C::kQBufs) - 1) & 1, abort_flag,
+                                 timeout_ns))
             return false;
-          mbar_arrive_expect_tx(smem_u32(&cc.q_full[qb]), kTileBytes);
-          tma_load_3d(sQ + qb * kTileBytes, &tm_q, smem_u32(&cc.q_full[qb]), 0, it.q0, it.bh);
+          mbar_arrive_expect_tx(smem_u32(&cc.q_full[qb]), C::kQBytes);
+#pragma unroll
+          for (int dc = 0; dc < C::kDChunks; ++dc)
+            tma_load_3d(sQ + qb * C::kQBytes + dc * (kBM * 128), &tm_q, smem_u32(&cc.q_full[qb]), dc * 64, it.q0,
+                        it.bh);
           ++q_count;
         }
         const int stage = gk % kStages;
@@ -354,8 +401,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             !mbar_wait_bounded(smem_u32(&cc.k_empty[stage]), ((gk / kStages) - 1) & 1, abort_flag, timeout_ns))
           return false;
         const int kt = cc.live[kc.i % kSlots][kc.t];
-        mbar_arrive_expect_tx(smem_u32(&cc.k_full[stage]), kTileBytes);
-        tma_load_3d(sK + stage * kTileBytes, &tm_k, smem_u32(&cc.k_full[stage]), 0, kt * kBN, it.bh);
+        mbar_arrive_expect_tx(smem_u32(&cc.k_full[stage]), C::kKVBytes);
+#pragma unroll
+        for (int dc = 0; dc < C::kDChunks; ++dc)
+          tma_load_3d(sK + stage * C::kKVBytes + dc * (kBN * 128), &tm_k, smem_u32(&cc.k_full[stage]), dc * 64,
+                      kt * kBN, it.bh);
         ++gk;
         return true;
       };
@@ -366,8 +416,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             !mbar_wait_bounded(smem_u32(&cc.v_empty[stage]), ((gv / kStages) - 1) & 1, abort_flag, timeout_ns))
           return false;
         const int kt = cc.live[vc.i % kSlots][vc.t];
-        mbar_arrive_expect_tx(smem_u32(&cc.v_full[stage]), kTileBytes);
-        tma_load_3d(sV + stage * kTileBytes, &tm_v, smem_u32(&cc.v_full[stage]), 0, kt * kBN, it.bh);
+        mbar_arrive_expect_tx(smem_u32(&cc.v_full[stage]), C::kKVBytes);
+#pragma unroll
+        for (int dc = 0; dc < C::kDChunks; ++dc)
+          tma_load_3d(sV + stage * C::kKVBytes + dc * (kBN * 128), &tm_v, smem_u32(&cc.v_full[stage]), dc * 64,
+                      kt * kBN, it.bh);
         ++gv;
         return true;
       };
@@ -399,8 +452,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           mbar_wait_bounded(smem_u32(&cc.k_full[x % kStages]), (x / kStages) & 1, &zero, timeout_ns);
         for (uint32_t x = (gv > static_cast<uint32_t>(kStages) ? gv - kStages : 0u); x < gv; ++x)
           mbar_wait_bounded(smem_u32(&cc.v_full[x % kStages]), (x / kStages) & 1, &zero, timeout_ns);
-        for (uint32_t q = (q_count > 2 ? q_count - 2 : 0u); q < q_count; ++q)
-          mbar_wait_bounded(smem_u32(&cc.q_full[q & 1]), (q >> 1) & 1, &zero, timeout_ns);
+        for (uint32_t q = (q_count > static_cast<uint32_t>(C::kQBufs) ? q_count - C::kQBufs : 0u); q < q_count; ++q)
+          mbar_wait_bounded(smem_u32(&cc.q_full[q % C::kQBufs]), (q / C::kQBufs) & 1, &zero, timeout_ns);
       }
     }
   } else if (warp == 10 || warp == 11) {
@@ -408,14 +461,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int c = warp - 10;
     ChainCtl& cc = ctl.ch[c];
     if (lane == 0) {
-      const uint32_t sQ = base + c * kChainBytes;
-      const uint32_t sK = sQ + 2 * kTileBytes;
-      const uint32_t sV = sK + kStages * kTileBytes;
+      const uint32_t sQ = base + c * C::kChainBytes;
+      const uint32_t sK = sQ + C::kQBufs * C::kQBytes;
+      const uint32_t sV = sK + kStages * C::kKVBytes;
       const uint32_t tS = tmem + c * kChainCols + kSCol;
       const uint32_t tP = tmem + c * kChainCols + kPCol;
       const uint32_t tO = tmem + c * kChainCols + kOCol;
       constexpr uint32_t idesc_qk = make_idesc_f16(kBM, kBN, BF16 ? 1 : 0, 0);
-      constexpr uint32_t idesc_pv = make_idesc_f16(kBM, kD, BF16 ? 1 : 0, 1);
+      constexpr uint32_t idesc_pv = make_idesc_f16(kBM, D, BF16 ? 1 : 0, 1);
       const int n_items = chain_items(c);
       bool ok = true;
 
@@ -425,8 +478,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto advance_qk = [&]() -> int {
         const int res = advance(cc, qc, n_items, true);
         if (res == 1 && qc.t == 0) {
-          qqb = q_count & 1;
-          if (!mbar_wait_bounded(smem_u32(&cc.q_full[qqb]), (q_count >> 1) & 1, abort_flag, timeout_ns))
+          qqb = q_count % C::kQBufs;
+          if (!mbar_wait_bounded(smem_u32(&cc.q_full[qqb]), (q_count / C::kQBufs) & 1, abort_flag, timeout_ns))
             return -1;
           ++q_count;
         }
@@ -440,12 +493,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         // S is free once the softmax has copied S of tile g-1 into registers.
         if (g > 0 && !mbar_wait_bounded(smem_u32(&cc.s_free), (g - 1) & 1, abort_flag, timeout_ns)) return false;
         tc_fence_after();
-        const uint32_t sQb = sQ + qqb * kTileBytes;
-        const uint32_t sKb = sK + stage * kTileBytes;
+        const uint32_t sQb = sQ + qqb * C::kQBytes;
+        const uint32_t sKb = sK + stage * C::kKVBytes;
 #pragma unroll
-        for (int kk = 0; kk < kD / 16; ++kk)
-          mma_ss(tS, smem_desc_sw128(sQb + kk * 32, 16, 1024), smem_desc_sw128(sKb + kk * 32, 16, 1024), idesc_qk,
+        for (int kk = 0; kk < D / 16; ++kk) {
+          // 16 head dims: swizzle chunk kk / 4 of the rows, 32 bytes into it.
+          const uint32_t qoff = (kk >> 2) * (kBM * 128) + (kk & 3) * 32;
+          const uint32_t koff = (kk >> 2) * (kBN * 128) + (kk & 3) * 32;
+          mma_ss(tS, smem_desc_sw128(sQb + qoff, 16, 1024), smem_desc_sw128(sKb + koff, 16, 1024), idesc_qk,
                  kk > 0 ? 1u : 0u);
+        }
         mma_commit(smem_u32(&cc.s_full));
         mma_commit(smem_u32(&cc.k_empty[stage]));
         if (qc.t + 1 == qc.n) mma_commit(smem_u32(&cc.q_empty[qqb]));  // last QK^T of the item
@@ -471,8 +528,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         tc_fence_after();
-        const uint32_t sVb = sV + stage * kTileBytes;
+        const uint32_t sVb = sV + stage * C::kKVBytes;
         const bool fresh = first_of[g & 1];
+        // V is MN-major: 16 keys are 2048 bytes into each 64-dim chunk; the
+        // chunks (D = 128) are kBN * 128 bytes apart.
 #pragma unroll
         for (int kk = 0; kk < kBN / 16; ++kk)
           mma_ts(tO, tP + kk * 8, smem_desc_sw128(sVb + kk * 2048, kBN * 128, 1024), idesc_pv,
@@ -493,11 +552,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     ChainCtl& cc = ctl.ch[c];
     const int r = threadIdx.x & 127;  // query row == TMEM lane
     const uint32_t t_lane = tmem + c * kChainCols + (static_cast<uint32_t>(wq * 32) << 16);
-    const uint32_t sO = base + c * kChainBytes + (2 + 2 * kStages) * kTileBytes;
-    uint8_t* out_row = smem + c * kChainBytes + (2 + 2 * kStages) * kTileBytes + r * 128;
+    // O staging tile (D = 64 only): after Q, K and V of the chain.
+    constexpr int kStageOff = C::kQBufs * C::kQBytes + 2 * kStages * C::kKVBytes;
+    const uint32_t sO = base + c * C::kChainBytes + kStageOff;
+    uint8_t* out_row = smem + c * C::kChainBytes + kStageOff + r * 128;
     const int n_items = chain_items(c);
     const int bar_id = 1 + c;
-    const int G4 = W >> 2;  // 16-byte groups per mask row (vec path: one per key tile)
+    const int G4 = W >> 2;  // 16-byte groups per mask row (vec path)
     bool ok = true;
     uint32_t g = 0;  // tiles processed by this chain
 
@@ -516,11 +577,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       return mask + (static_cast<int64_t>(it.bh) * N + it.q0 + r) * W;
     };
     // Mask words of key tile kt for this thread's row of `it` (0 for padding rows).
-    auto fetch_words = [&](const Item& it, int kt, uint32_t (&mw)[4]) {
+    auto fetch_words = [&](const Item& it, int kt, uint32_t (&mw)[kWords]) {
       if (r < it.rows_valid) {
-        load_tile_words(row_ptr(it), kt, W, N, vec != 0, mw);
+        load_tile_words<D>(row_ptr(it), kt, W, N, vec != 0, mw);
       } else {
-        mw[0] = mw[1] = mw[2] = mw[3] = 0u;
+#pragma unroll
+        for (int w = 0; w < kWords; ++w) mw[w] = 0u;
       }
     };
     // This thread's packed-mask row of `it` into L1 (a prefetch holds no registers).
@@ -543,10 +605,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int u = 0; u < kScanBatch; ++u)
             v[u] = (gb + u < G4) ? __ldg(reinterpret_cast<const uint4*>(mrow) + gb + u) : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-          for (int u = 0; u < kScanBatch; ++u) set_live(gb + u, group_or(v[u], gb + u, N), bits);
+          for (int u = 0; u < kScanBatch; ++u)
+            if (gb + u < G4) group_live<D>(v[u], gb + u, N, bits);
         }
       } else {
-        for (int cw = g0 * 4; cw < W; ++cw) set_live(cw >> 2, __ldg(mrow + cw) & valid_bits(cw, N), bits);
+        for (int cw = g0 * 4; cw < W; ++cw) set_live(cw / kWords, __ldg(mrow + cw) & valid_bits(cw, N), bits);
       }
     };
     // Stores this warp's share of item j's live bits (before a WG barrier).
@@ -605,7 +668,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (r == 0) publish(j);
     }
 
-    uint32_t mw[4] = {0u, 0u, 0u, 0u};
+    uint32_t mw[kWords] = {};
     bool have_mw = false;  // mw already holds tile 0 of the current item
     for (int i = 0; i < n_items; ++i) {
       const int slot = i % kSlots;
@@ -634,13 +697,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         float s[kBN];
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) tmem_ld32f(t_lane + kSCol + ch * 32, s + ch * 32);
+        for (int ch = 0; ch < kWords; ++ch) tmem_ld32f(t_lane + kSCol + ch * 32, s + ch * 32);
         tmem_wait_ld();
         arrive_warp(cc.s_free);  // the next QK^T may overwrite S now
 
         float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
+        for (int ch = 0; ch < kWords; ++ch) {
           const uint32_t word = mw[ch];
 #pragma unroll
           for (int jj = 0; jj < 32; jj += 2) {
@@ -684,7 +747,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float la[2] = {0.f, 0.f};
         uint64_t lr2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
 #pragma unroll
-        for (int ch = 0; ch < 4; ++ch) {
+        for (int ch = 0; ch < kWords; ++ch) {
           uint32_t pk[16];
 #pragma unroll
           for (int jj = 0; jj < 16; ++jj) {
@@ -706,7 +769,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           // Rare: the running max rose by more than the threshold; bring O
           // (PV of tiles before g, complete) to the new max before PV of g.
 #pragma unroll 1
-          for (int ch = 0; ch < kD / 16; ++ch) {
+          for (int ch = 0; ch < D / 16; ++ch) {
             uint32_t u[16];
             tmem_ld16(t_lane + kOCol + ch * 16, u);
             tmem_wait_ld();
@@ -732,51 +795,91 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool do_scan = i + 2 < n_items;
       const Item itn = item_of(chain_item(c, do_scan ? i + 2 : i), BH, QT, N);
       if (do_scan && occ == nullptr) prefetch_rows_l1(itn);
-      // O of the item, normalised and packed to 16-bit pairs (32 words per row).
       const float inv = (l_out > 0.f) ? (1.f / l_out) : 0.f;
-      uint32_t h[32];
-      if (ok && n > 0 && wait_all(cc.pv_done, (g - 1) & 1)) {
+      const bool o_ready = ok && n > 0 && wait_all(cc.pv_done, (g - 1) & 1);
+      if (n > 0 && !o_ready) ok = false;
+      const float lse_row = (l_run > 0.f) ? (m_run + log2f(l_run)) * kLn2 : -FLT_MAX;
+      if constexpr (C::kStageO) {
+        // O of the item, normalised and packed to 16-bit pairs (32 words per
+        // row), through the staging tile and one TMA store.
+        uint32_t h[32];
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           uint32_t u[32];
-          tmem_ld32(t_lane + kOCol + half * 32, u);
-          tmem_wait_ld();
+          if (o_ready) {
+            tmem_ld32(t_lane + kOCol + half * 32, u);
+            tmem_wait_ld();
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) u[e] = 0u;
+          }
 #pragma unroll
           for (int e = 0; e < 16; ++e)
             h[half * 16 + e] = pack2<BF16>(__uint_as_float(u[2 * e]) * inv, __uint_as_float(u[2 * e + 1]) * inv);
         }
-      } else {
-        if (n > 0) ok = false;
-#pragma unroll
-        for (int e = 0; e < 32; ++e) h[e] = 0u;
-      }
-      if (do_scan && occ == nullptr) {
-        LiveBits bits{};
-        scan_rest(itn, 0, bits);
-        post_part(i + 2, bits);
-      }
-      // The previous item's O store must have finished reading the staging tile.
-      if (r == 0) bulk_wait_group_read0();
-      named_bar_sync(bar_id, 128);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        const int chunk = q ^ (r & 7);  // 128-byte swizzle of the O tensor map
-        *reinterpret_cast<uint4*>(out_row + chunk * 16) = make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
-      }
-      if (lse != nullptr && r < it.rows_valid)
-        lse[static_cast<int64_t>(it.bh) * N + it.q0 + r] = (l_run > 0.f) ? (m_run + log2f(l_run)) * kLn2 : -FLT_MAX;
-      fence_proxy_async_smem();
-      named_bar_sync(bar_id, 128);
-      if (r == 0) {
-        if (ctl.abort_flag == 0) {
-          tma_store_3d(&tm_o, sO, 0, it.q0, it.bh);
-          bulk_commit_group();
+        if (do_scan && occ == nullptr) {
+          LiveBits bits{};
+          scan_rest(itn, 0, bits);
+          post_part(i + 2, bits);
         }
-        if (do_scan) publish(i + 2);
+        // The previous item's O store must have finished reading the staging tile.
+        if (r == 0) bulk_wait_group_read0();
+        named_bar_sync(bar_id, 128);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          const int chunk = q ^ (r & 7);  // 128-byte swizzle of the O tensor map
+          *reinterpret_cast<uint4*>(out_row + chunk * 16) =
+              make_uint4(h[4 * q], h[4 * q + 1], h[4 * q + 2], h[4 * q + 3]);
+        }
+        if (lse != nullptr && r < it.rows_valid) lse[static_cast<int64_t>(it.bh) * N + it.q0 + r] = lse_row;
+        fence_proxy_async_smem();
+        named_bar_sync(bar_id, 128);
+        if (r == 0) {
+          if (ctl.abort_flag == 0) {
+            tma_store_3d(&tm_o, sO, 0, it.q0, it.bh);
+            bulk_commit_group();
+          }
+          if (do_scan) publish(i + 2);
+        }
+      } else {
+        // O of the item, normalised, stored from registers 32 columns (64
+        // bytes of the row) at a time.
+        uint16_t* orow = out + (static_cast<int64_t>(it.bh) * N + it.q0 + r) * D;
+        const bool store = r < it.rows_valid && ctl.abort_flag == 0;
+#pragma unroll 1
+        for (int dc = 0; dc < D / 32; ++dc) {
+          uint32_t u[32];
+          if (o_ready) {
+            tmem_ld32(t_lane + kOCol + dc * 32, u);
+            tmem_wait_ld();
+          } else {
+#pragma unroll
+            for (int e = 0; e < 32; ++e) u[e] = 0u;
+          }
+          uint32_t hw[16];
+#pragma unroll
+          for (int e = 0; e < 16; ++e)
+            hw[e] = pack2<BF16>(__uint_as_float(u[2 * e]) * inv, __uint_as_float(u[2 * e + 1]) * inv);
+          if (store) {
+            uint4* dst = reinterpret_cast<uint4*>(orow + dc * 32);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) dst[q] = make_uint4(hw[4 * q], hw[4 * q + 1], hw[4 * q + 2], hw[4 * q + 3]);
+          }
+        }
+        if (lse != nullptr && r < it.rows_valid) lse[static_cast<int64_t>(it.bh) * N + it.q0 + r] = lse_row;
+        if (do_scan && occ == nullptr) {
+          LiveBits bits{};
+          scan_rest(itn, 0, bits);
+          post_part(i + 2, bits);
+        }
+        named_bar_sync(bar_id, 128);
+        if (r == 0 && do_scan) publish(i + 2);
       }
     }
     if (!ok && lane == 0) fail();
-    if (r == 0) bulk_wait_group_read0();
+    if constexpr (C::kStageO) {
+      if (r == 0) bulk_wait_group_read0();
+    }
   }
 
   tc_fence_before();
@@ -801,13 +904,14 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// [BH, N, 64] view of a contiguous [B, H, N, 64] tensor, 128-row boxes, 128-byte swizzle.
-bool map3d(CUtensorMap* m, const void* ptr, int dtype, int64_t BH, int64_t N) {
+// [BH, N, D] view of a contiguous [B, H, N, D] tensor: boxes of 64 head dims
+// (one 128-byte swizzle span) by `rows` rows.
+bool map3d(CUtensorMap* m, const void* ptr, int dtype, int64_t D, int64_t BH, int64_t N, int rows) {
   auto fn = encode_fn();
   if (fn == nullptr) return false;
-  cuuint64_t dims[3] = {static_cast<cuuint64_t>(kD), static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(BH)};
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(kD * 2), static_cast<cuuint64_t>(N * kD * 2)};
-  cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(kBM), 1u};
+  cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(BH)};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(D * 2), static_cast<cuuint64_t>(N * D * 2)};
+  cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(rows), 1u};
   cuuint32_t estr[3] = {1u, 1u, 1u};
   return fn(m, dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
             const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
@@ -815,12 +919,14 @@ bool map3d(CUtensorMap* m, const void* ptr, int dtype, int64_t BH, int64_t N) {
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <bool BF16>
+template <int D, bool BF16>
 int launch(const AttnParams& p, const char** msg) {
+  using C = ChainCfg<D>;
+  constexpr size_t kSmemBytes = smem_bytes<D>();
   const int64_t BH = p.B * p.H;
   const int64_t N = p.N;
   const int64_t W = (N + 31) / 32;
-  const int64_t KT = (N + kBN - 1) / kBN;
+  const int64_t KT = (N + C::kBN - 1) / C::kBN;
   const int64_t QT = (N + kBM - 1) / kBM;
   const int64_t total = QT * BH;
   if (total > 0x3FFFFFFFll) {
@@ -828,8 +934,8 @@ int launch(const AttnParams& p, const char** msg) {
     return kErrArg;
   }
   CUtensorMap mq, mk, mv, mo;
-  if (!map3d(&mq, p.q, p.dtype, BH, N) || !map3d(&mk, p.k, p.dtype, BH, N) || !map3d(&mv, p.v, p.dtype, BH, N) ||
-      !map3d(&mo, p.out, p.dtype, BH, N)) {
+  if (!map3d(&mq, p.q, p.dtype, D, BH, N, kBM) || !map3d(&mk, p.k, p.dtype, D, BH, N, C::kBN) ||
+      !map3d(&mv, p.v, p.dtype, D, BH, N, C::kBN) || !map3d(&mo, p.out, p.dtype, D, BH, N, kBM)) {
     *msg = "attention: cuTensorMapEncodeTiled failed (pointer alignment or driver entry point)";
     return kErrCuda;
   }
@@ -844,7 +950,7 @@ int launch(const AttnParams& p, const char** msg) {
     *msg = "attention: cannot query the SM count";
     return kErrCuda;
   }
-  auto kern = attn_fwd_chain_kernel<BF16>;
+  auto kern = attn_fwd_chain_kernel<D, BF16>;
   if (!smem_set[dev]) {
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
@@ -856,8 +962,10 @@ int launch(const AttnParams& p, const char** msg) {
   }
   const int vec = (W % 4 == 0 && (reinterpret_cast<uintptr_t>(p.mask) & 15u) == 0) ? 1 : 0;
   const int grid = static_cast<int>(total < sms[dev] ? total : sms[dev]);
+  // The occupancy map describes 128-key tiles: only the D = 64 kernel uses it.
+  const uint32_t* occ = D == 64 ? p.occ : nullptr;
   cudaError_t e = launch_pdl(kern, static_cast<unsigned>(grid), kThreads, kSmemBytes, p.stream, mq, mk, mv, mo,
-                             p.mask, p.occ, p.lse, static_cast<int>(N), static_cast<int>(BH), static_cast<int>(W),
+                             static_cast<uint16_t*>(p.out), p.mask, occ, p.lse, static_cast<int>(N), static_cast<int>(BH), static_cast<int>(W),
                              static_cast<int>(KT), static_cast<int>(total), vec, p.scale * kLog2e, p.err_word,
                              p.timeout_ns);
   if (e == cudaSuccess) e = cudaGetLastError();
@@ -875,10 +983,13 @@ int launch(const AttnParams& p, const char** msg) {
 
 }  // namespace
 
-bool chain_supported(const AttnParams& p) { return p.D == kD && p.N <= kMaxTiles * kBN; }
+bool chain_supported(const AttnParams& p) {
+  return (p.D == 64 && p.N <= ChainCfg<64>::kMaxN) || (p.D == 128 && p.N <= ChainCfg<128>::kMaxN);
+}
 
 int launch_attn_fwd_chain(const AttnParams& p, const char** msg) {
-  return p.dtype == 1 ? launch<true>(p, msg) : launch<false>(p, msg);
+  if (p.D == 128) return p.dtype == 1 ? launch<128, true>(p, msg) : launch<128, false>(p, msg);
+  return p.dtype == 1 ? launch<64, true>(p, msg) : launch<64, false>(p, msg);
 }
 
 }  // namespace sma

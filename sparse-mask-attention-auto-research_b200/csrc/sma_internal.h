@@ -73,8 +73,8 @@ cudaError_t launch_pdl(void (*kern)(Params...), unsigned grid, unsigned block, s
   return cudaLaunchKernelEx(&cfg, kern, static_cast<Params>(args)...);
 }
 
-// Persistent two-chain kernel (attn_fwd_chain.cu): head dim 64, any
-// supported N.  launch_attn_fwd dispatches to it when chain_supported().
+// Persistent two-chain kernel (attn_fwd_chain.cu): head dims 64 and 128, N up
+// to 16384 / 8192.  launch_attn_fwd dispatches to it when chain_supported().
 bool chain_supported(const AttnParams& p);
 int launch_attn_fwd_chain(const AttnParams& p, const char** msg);
 
