@@ -62,6 +62,7 @@ constexpr int kStages = 2;         // K ring and V ring depth per chain
 constexpr int kTmemCols = 512;
 constexpr int kChainCols = 256;
 constexpr int kScanBatch = 4;      // 16-byte mask loads in flight per thread while scanning
+constexpr int kEpiGroups = 8;      // D = 128: mask rows of up to 8 16-byte groups (N <= 1024) scanned from registers
 
 // Per head dim: D = 64 takes 128-key tiles, D = 128 takes 64-key tiles, so a
 // K or V tile is 16 KiB either way and S + P + O of a chain fit its 256 TMEM
@@ -219,6 +220,13 @@ __device__ __forceinline__ void load_tile_words(const uint32_t* mrow, int kt, in
   }
 }
 
+// Eight 32-bit words r[o .. o+7] to a 32-byte aligned global address.
+__device__ __forceinline__ void st_global_v8(void* dst, const uint32_t (&r)[16], int o) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(dst), "r"(r[o]), "r"(r[o + 1]),
+               "r"(r[o + 2]), "r"(r[o + 3]), "r"(r[o + 4]), "r"(r[o + 5]), "r"(r[o + 6]), "r"(r[o + 7])
+               : "memory");
+}
+
 // Live-tile bits of one item (bit t = key tile t), kept in registers.
 struct LiveBits {
   uint32_t w[kLiveWords];
@@ -259,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                           const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
                           uint16_t* __restrict__ out, const uint32_t* __restrict__ mask,
                           const uint32_t* __restrict__ occ, float* __restrict__ lse, int N, int BH, int W,
-                          int KT, int total_items, int vec, float scale_log2, uint32_t* err_word,
+                          int KT, int total_items, int vec, int o_wide, float scale_log2, uint32_t* err_word,
                           uint64_t timeout_ns) {
   using C = ChainCfg<D>;
   constexpr int kBN = C::kBN;
@@ -620,12 +628,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) cc.part[j % kSlots][wq][k] = x;
       }
     };
-    // Thread 0 of the WG, after a WG barrier: builds item j's live list and publishes it.
+    // Warp 0 of the WG, after a WG barrier: builds item j's live list (one
+    // lane per key tile of each 32-tile word, ranks by popcount) and publishes it.
     auto publish = [&](int j) {
       const int slot = j % kSlots;
-      if (j >= kSlots &&
-          !mbar_wait_bounded(smem_u32(&cc.sched_empty[slot]), ((j / kSlots) - 1) & 1, abort_flag, timeout_ns)) {
-        fail();
+      if (j >= kSlots && !wait_all(cc.sched_empty[slot], ((j / kSlots) - 1) & 1)) {
+        if (lane == 0) fail();
         return;
       }
       // Live key tiles straight from the packer's occupancy map when there is
@@ -643,14 +651,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         } else {
           x = cc.part[slot][0][k] | cc.part[slot][1][k] | cc.part[slot][2][k] | cc.part[slot][3][k];
         }
-        while (x != 0u) {  // set bits in increasing key-tile order
-          const int b = __ffs(x) - 1;
-          x &= x - 1u;
-          if (k * 32 + b < KT) cc.live[slot][n++] = static_cast<uint16_t>(k * 32 + b);
-        }
+        if (KT - k * 32 < 32) x &= (1u << (KT - k * 32)) - 1u;
+        if ((x >> lane) & 1u)  // set bits in increasing key-tile order
+          cc.live[slot][n + __popc(x & ((1u << lane) - 1u))] = static_cast<uint16_t>(k * 32 + lane);
+        n += __popc(x);
       }
-      cc.n_live[slot] = n;
-      mbar_arrive(smem_u32(&cc.sched_full[slot]));
+      __syncwarp();
+      if (lane == 0) {
+        cc.n_live[slot] = n;
+        mbar_arrive(smem_u32(&cc.sched_full[slot]));
+      }
     };
 
     // Prologue: the live lists of the first two items.  The second item's
@@ -665,7 +675,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         post_part(j, bits);
       }
       named_bar_sync(bar_id, 128);
-      if (r == 0) publish(j);
+      if (wq == 0) publish(j);
     }
 
     uint32_t mw[kWords] = {};
@@ -794,7 +804,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       // registers).
       const bool do_scan = i + 2 < n_items;
       const Item itn = item_of(chain_item(c, do_scan ? i + 2 : i), BH, QT, N);
-      if (do_scan && occ == nullptr) prefetch_rows_l1(itn);
+      // D = 128 loads short rows (up to kEpiGroups 16-byte groups) outright
+      // below, before it writes O.
+      const bool scan_regs = !C::kStageO && vec && G4 <= kEpiGroups;
+      if (do_scan && occ == nullptr && !scan_regs) prefetch_rows_l1(itn);
       const float inv = (l_out > 0.f) ? (1.f / l_out) : 0.f;
       const bool o_ready = ok && n > 0 && wait_all(cc.pv_done, (g - 1) & 1);
       if (n > 0 && !o_ready) ok = false;
@@ -834,16 +847,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lse != nullptr && r < it.rows_valid) lse[static_cast<int64_t>(it.bh) * N + it.q0 + r] = lse_row;
         fence_proxy_async_smem();
         named_bar_sync(bar_id, 128);
-        if (r == 0) {
-          if (ctl.abort_flag == 0) {
-            tma_store_3d(&tm_o, sO, 0, it.q0, it.bh);
-            bulk_commit_group();
-          }
-          if (do_scan) publish(i + 2);
+        if (r == 0 && ctl.abort_flag == 0) {
+          tma_store_3d(&tm_o, sO, 0, it.q0, it.bh);
+          bulk_commit_group();
         }
+        if (wq == 0 && do_scan) publish(i + 2);
       } else {
+        // The scan loads of item i+2 go first and land while O is written.
+        uint4 sv[kEpiGroups];
+        const bool load_sv = scan_regs && do_scan && occ == nullptr && r < itn.rows_valid;
+#pragma unroll
+        for (int u = 0; u < kEpiGroups; ++u)
+          sv[u] = (load_sv && u < G4) ? __ldg(reinterpret_cast<const uint4*>(row_ptr(itn)) + u)
+                                      : make_uint4(0u, 0u, 0u, 0u);
         // O of the item, normalised, stored from registers 32 columns (64
-        // bytes of the row) at a time.
+        // bytes of the row) at a time, as two 32-byte stores when `out` allows.
         uint16_t* orow = out + (static_cast<int64_t>(it.bh) * N + it.q0 + r) * D;
         const bool store = r < it.rows_valid && ctl.abort_flag == 0;
 #pragma unroll 1
@@ -861,19 +879,30 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 16; ++e)
             hw[e] = pack2<BF16>(__uint_as_float(u[2 * e]) * inv, __uint_as_float(u[2 * e + 1]) * inv);
           if (store) {
-            uint4* dst = reinterpret_cast<uint4*>(orow + dc * 32);
+            if (o_wide) {
+              st_global_v8(orow + dc * 32, hw, 0);
+              st_global_v8(orow + dc * 32 + 16, hw, 8);
+            } else {
+              uint4* dst = reinterpret_cast<uint4*>(orow + dc * 32);
 #pragma unroll
-            for (int q = 0; q < 4; ++q) dst[q] = make_uint4(hw[4 * q], hw[4 * q + 1], hw[4 * q + 2], hw[4 * q + 3]);
+              for (int q = 0; q < 4; ++q) dst[q] = make_uint4(hw[4 * q], hw[4 * q + 1], hw[4 * q + 2], hw[4 * q + 3]);
+            }
           }
         }
         if (lse != nullptr && r < it.rows_valid) lse[static_cast<int64_t>(it.bh) * N + it.q0 + r] = lse_row;
         if (do_scan && occ == nullptr) {
           LiveBits bits{};
-          scan_rest(itn, 0, bits);
+          if (scan_regs) {
+#pragma unroll
+            for (int u = 0; u < kEpiGroups; ++u)
+              if (u < G4) group_live<D>(sv[u], u, N, bits);
+          } else {
+            scan_rest(itn, 0, bits);
+          }
           post_part(i + 2, bits);
         }
         named_bar_sync(bar_id, 128);
-        if (r == 0 && do_scan) publish(i + 2);
+        if (wq == 0 && do_scan) publish(i + 2);
       }
     }
     if (!ok && lane == 0) fail();
@@ -961,12 +990,13 @@ int launch(const AttnParams& p, const char** msg) {
     smem_set[dev] = true;
   }
   const int vec = (W % 4 == 0 && (reinterpret_cast<uintptr_t>(p.mask) & 15u) == 0) ? 1 : 0;
+  const int o_wide = (reinterpret_cast<uintptr_t>(p.out) & 31u) == 0 ? 1 : 0;  // 32-byte O stores (D = 128)
   const int grid = static_cast<int>(total < sms[dev] ? total : sms[dev]);
   // The occupancy map describes 128-key tiles: only the D = 64 kernel uses it.
   const uint32_t* occ = D == 64 ? p.occ : nullptr;
   cudaError_t e = launch_pdl(kern, static_cast<unsigned>(grid), kThreads, kSmemBytes, p.stream, mq, mk, mv, mo,
                              static_cast<uint16_t*>(p.out), p.mask, occ, p.lse, static_cast<int>(N), static_cast<int>(BH), static_cast<int>(W),
-                             static_cast<int>(KT), static_cast<int>(total), vec, p.scale * kLog2e, p.err_word,
+                             static_cast<int>(KT), static_cast<int>(total), vec, o_wide, p.scale * kLog2e, p.err_word,
                              p.timeout_ns);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
