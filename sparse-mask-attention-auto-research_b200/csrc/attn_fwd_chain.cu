@@ -174,12 +174,21 @@ struct Item {
   int bh, q0, rows_valid;
 };
 
-// Item w: query tiles in decreasing index order (under a causal mask the
-// last query tiles see the most keys), batch*head fastest.
-__device__ __forceinline__ Item item_of(int w, int BH, int QT, int N) {
+// Item w.  Query tiles run in decreasing index order: under a causal mask
+// the last query tiles see the most keys.
+//   head_major == 0: batch*head fastest, so all chains of a round work on the
+//     same query tile index and causal rounds are even.  Used when K and V of
+//     all heads fit in L2 together.
+//   head_major != 0: the query tiles of one batch*head are consecutive, so the
+//     chains working on them at the same time share that head's K and V in
+//     L2 (the serpentine walk still pairs a chain's heavy tiles with light
+//     ones).  Used when K and V would not stay in L2 between rounds.
+__device__ __forceinline__ Item item_of(int w, int BH, int QT, int N, int head_major) {
   Item it;
-  const int qt = QT - 1 - w / BH;
-  it.bh = w % BH;
+  const int fast_n = head_major ? QT : BH;  // one division for either order
+  const int slow = w / fast_n, fast = w - slow * fast_n;
+  const int qt = QT - 1 - (head_major ? fast : slow);
+  it.bh = head_major ? slow : fast;
   it.q0 = qt * kBM;
   it.rows_valid = min(kBM, N - it.q0);
   return it;
@@ -267,7 +276,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                           const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
                           uint16_t* __restrict__ out, const uint32_t* __restrict__ mask,
                           const uint32_t* __restrict__ occ, float* __restrict__ lse, int N, int BH, int W,
-                          int KT, int total_items, int vec, int o_wide, float scale_log2, uint32_t* err_word,
+                          int KT, int total_items, int vec, int o_wide, int head_major, float scale_log2,
+                          uint32_t* err_word,
                           uint64_t timeout_ns) {
   using C = ChainCfg<D>;
   constexpr int kBN = C::kBN;
@@ -389,7 +399,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t gk = 0, gv = 0, q_count = 0;  // K, V and Q copies issued
       bool ok = true;
       auto issue_k = [&]() -> bool {
-        const Item it = item_of(chain_item(c, kc.i), BH, QT, N);
+        const Item it = item_of(chain_item(c, kc.i), BH, QT, N, head_major);
         if (kc.t == 0) {
           // First tile of an item: its Q, into the buffer the item kQBufs back used.
           const int qb = q_count % C::kQBufs;
@@ -418,7 +428,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         return true;
       };
       auto issue_v = [&]() -> bool {
-        const Item it = item_of(chain_item(c, vc.i), BH, QT, N);
+        const Item it = item_of(chain_item(c, vc.i), BH, QT, N, head_major);
         const int stage = gv % kStages;
         if (gv >= static_cast<uint32_t>(kStages) &&
             !mbar_wait_bounded(smem_u32(&cc.v_empty[stage]), ((gv / kStages) - 1) & 1, abort_flag, timeout_ns))
@@ -640,7 +650,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // one (two words per item: the map is only made for N <= 8192).
       const uint32_t* occ_j = nullptr;
       if (occ != nullptr) {
-        const Item itj = item_of(chain_item(c, j), BH, QT, N);
+        const Item itj = item_of(chain_item(c, j), BH, QT, N, head_major);
         occ_j = occ + 2 * (static_cast<int64_t>(itj.bh) * QT + itj.q0 / kBM);
       }
       uint32_t n = 0;
@@ -667,11 +677,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     // mask rows are prefetched into L1 first, so both rows are fetched from
     // HBM at once, and the first list is published before the second is built.
     const int n_pre = n_items < 2 ? n_items : 2;
-    if (n_pre > 1 && occ == nullptr) prefetch_rows_l1(item_of(chain_item(c, 1), BH, QT, N));
+    if (n_pre > 1 && occ == nullptr) prefetch_rows_l1(item_of(chain_item(c, 1), BH, QT, N, head_major));
     for (int j = 0; j < n_pre; ++j) {
       if (occ == nullptr) {
         LiveBits bits{};
-        scan_rest(item_of(chain_item(c, j), BH, QT, N), 0, bits);
+        scan_rest(item_of(chain_item(c, j), BH, QT, N, head_major), 0, bits);
         post_part(j, bits);
       }
       named_bar_sync(bar_id, 128);
@@ -682,7 +692,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool have_mw = false;  // mw already holds tile 0 of the current item
     for (int i = 0; i < n_items; ++i) {
       const int slot = i % kSlots;
-      const Item it = item_of(chain_item(c, i), BH, QT, N);
+      const Item it = item_of(chain_item(c, i), BH, QT, N, head_major);
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&cc.sched_full[slot]), (i / kSlots) & 1,
                                                               abort_flag, timeout_ns));
       const uint32_t n = ok ? cc.n_live[slot] : 0u;
@@ -728,7 +738,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (t + 1 < n) {
           fetch_words(it, cc.live[slot][t + 1], mw);
         } else if (next_kt >= 0) {
-          fetch_words(item_of(chain_item(c, i + 1), BH, QT, N), next_kt, mw);
+          fetch_words(item_of(chain_item(c, i + 1), BH, QT, N, head_major), next_kt, mw);
           have_mw = true;
         }
 
@@ -803,7 +813,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // wait for the last PV, so the loads after it hit (a prefetch holds no
       // registers).
       const bool do_scan = i + 2 < n_items;
-      const Item itn = item_of(chain_item(c, do_scan ? i + 2 : i), BH, QT, N);
+      const Item itn = item_of(chain_item(c, do_scan ? i + 2 : i), BH, QT, N, head_major);
       // D = 128 loads short rows (up to kEpiGroups 16-byte groups) outright
       // below, before it writes O.
       const bool scan_regs = !C::kStageO && vec && G4 <= kEpiGroups;
@@ -991,12 +1001,20 @@ int launch(const AttnParams& p, const char** msg) {
   }
   const int vec = (W % 4 == 0 && (reinterpret_cast<uintptr_t>(p.mask) & 15u) == 0) ? 1 : 0;
   const int o_wide = (reinterpret_cast<uintptr_t>(p.out) & 31u) == 0 ? 1 : 0;  // 32-byte O stores (D = 128)
+  // Head-major item order once K and V of all heads exceed half of L2.
+  static int l2_bytes[kMaxDevices] = {};
+  if (l2_bytes[dev] == 0 && cudaDeviceGetAttribute(&l2_bytes[dev], cudaDevAttrL2CacheSize, dev) != cudaSuccess) {
+    *msg = "attention: cannot query the L2 size";
+    return kErrCuda;
+  }
+  const int head_major = 2 * BH * N * D * 2 > l2_bytes[dev] / 2 ? 1 : 0;
   const int grid = static_cast<int>(total < sms[dev] ? total : sms[dev]);
   // The occupancy map describes 128-key tiles: only the D = 64 kernel uses it.
   const uint32_t* occ = D == 64 ? p.occ : nullptr;
   cudaError_t e = launch_pdl(kern, static_cast<unsigned>(grid), kThreads, kSmemBytes, p.stream, mq, mk, mv, mo,
                              static_cast<uint16_t*>(p.out), p.mask, occ, p.lse, static_cast<int>(N), static_cast<int>(BH), static_cast<int>(W),
-                             static_cast<int>(KT), static_cast<int>(total), vec, o_wide, p.scale * kLog2e, p.err_word,
+                             static_cast<int>(KT), static_cast<int>(total), vec, o_wide, head_major,
+                             p.scale * kLog2e, p.err_word,
                              p.timeout_ns);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
