@@ -36,10 +36,9 @@ extern "C" {
 #define SMA_DTYPE_FP16 0
 #define SMA_DTYPE_BF16 1
 
-/* Longest supported sequence: 16384 at head dim 64, 8192 at head dim 128;
- * the occupancy map (sma_pack_mask_occupancy) covers N <= 8192. */
-#define SMA_MAX_SEQ_LEN 16384
-#define SMA_MAX_SEQ_LEN_D128 8192
+/* Longest supported sequence (both head dims); the occupancy map
+ * (sma_pack_mask_occupancy) covers N <= 8192. */
+#define SMA_MAX_SEQ_LEN 65536
 #define SMA_MAX_SEQ_LEN_OCCUPANCY 8192
 
 #if defined(__GNUC__)
@@ -70,8 +69,7 @@ SMA_API int sma_pack_mask(const void* mask, void* packed, int64_t B, int64_t H, 
  * the scaled scores, or NULL to skip it (the reference's is_training=false).
  * Rows with no set bit get out = 0 and lse = -FLT_MAX (the reference CUDA
  * convention, csrc/sparse_attention.cu:133,141).
- * Supported: D in {64, 128}, 1 <= N <= SMA_MAX_SEQ_LEN (D = 64) or
- * SMA_MAX_SEQ_LEN_D128 (D = 128), 16-byte aligned
+ * Supported: D in {64, 128}, 1 <= N <= SMA_MAX_SEQ_LEN, 16-byte aligned
  * q/k/v/out, scale finite and > 0 (the kernels fold the scale into the
  * exponent after the masked row max; the reference always passes 1/sqrt(D)).
  *

@@ -38,8 +38,8 @@ int launch_attn_fwd(const AttnParams& p, const char** msg) {
     *msg = "attention: head dim must be 64 or 128";
     return kErrUnsupportedD;
   }
-  if (p.N > kMaxSeqLen || (p.D == 128 && p.N > kMaxSeqLenD128)) {
-    *msg = "attention: sequence length above the supported maximum (16384 for head dim 64, 8192 for 128)";
+  if (p.N > kMaxSeqLen) {
+    *msg = "attention: sequence length above the supported maximum (65536)";
     return kErrUnsupportedN;
   }
   if (p.occ != nullptr && p.N > kMaxSeqLenOcc) {

@@ -56,8 +56,8 @@ namespace {
 constexpr int kBM = 128;
 constexpr int kThreads = 384;
 constexpr int kSlots = 4;          // live-list slots per chain
-constexpr int kMaxTiles = 128;     // key tiles per item: N <= 16384 (D = 64), N <= 8192 (D = 128)
-constexpr int kLiveWords = kMaxTiles / 32;  // live-tile bit words per item
+constexpr int kMaxSeq = 65536;     // longest sequence the live-tile bitsets cover
+constexpr int kLiveWords = kMaxSeq / 64 / 32;  // bit words per item: one bit per key tile (64 keys or more)
 constexpr int kStages = 2;         // K ring and V ring depth per chain
 constexpr int kTmemCols = 512;
 constexpr int kChainCols = 256;
@@ -73,6 +73,7 @@ struct ChainCfg {
   static constexpr int kBN = D == 64 ? 128 : 64;       // keys per tile
   static constexpr int kWords = kBN / 32;              // packed-mask words of a row per tile
   static constexpr int kTilesPerGroup = 4 / kWords;    // tiles per 16-byte group of a mask row
+  static constexpr int kGroupsPerWord = 32 / kTilesPerGroup;  // groups per 32-tile bit word
   static constexpr int kDChunks = D / 64;
   static constexpr int kQBytes = kBM * D * 2;          // 16 / 32 KiB
   static constexpr int kKVBytes = kBN * D * 2;         // 16 KiB
@@ -85,7 +86,7 @@ struct ChainCfg {
   static constexpr int kPCol = kBN;
   static constexpr int kOCol = kBN + kBN / 2;
   static_assert(kOCol + D <= kChainCols, "TMEM budget");
-  static constexpr int kMaxN = kMaxTiles * kBN;
+  static constexpr int kMaxN = kMaxSeq;
 };
 constexpr float kRescaleThreshold = 8.0f;
 constexpr float kLn2 = 0.69314718055994530942f;
@@ -106,9 +107,12 @@ struct ChainCtl {
   uint64_t p_full;
   uint64_t pv_done;
   uint64_t drain;
-  uint32_t part[kSlots][4][kLiveWords];  // per-warp live-tile bits of the item being scanned
+  // Live key tiles of the items in flight, one bit per tile: the scan ORs
+  // each warp's bits into scan_bits, the publisher moves them to live_bits
+  // (clearing scan_bits) once the slot's previous item has been released.
+  uint32_t scan_bits[kSlots][kLiveWords];
+  uint32_t live_bits[kSlots][kLiveWords];
   uint32_t n_live[kSlots];
-  uint16_t live[kSlots][kMaxTiles];
 };
 
 struct Ctl {
@@ -236,30 +240,18 @@ __device__ __forceinline__ void st_global_v8(void* dst, const uint32_t (&r)[16],
                : "memory");
 }
 
-// Live-tile bits of one item (bit t = key tile t), kept in registers.
-struct LiveBits {
-  uint32_t w[kLiveWords];
-};
-
-__device__ __forceinline__ void set_live(int g, uint32_t x, LiveBits& b) {
-  if (x != 0u) {
-    const uint32_t m = 1u << (g & 31);
-#pragma unroll
-    for (int k = 0; k < kLiveWords; ++k) b.w[k] |= (g >> 5) == k ? m : 0u;  // no dynamic register index
-  }
-}
-
-// Live bits of the key tiles in 16-byte group g of a mask row (words 4g ..
-// 4g+3: one 128-key tile, or two 64-key tiles), columns >= N cleared.
+// Live bits, relative to tile 32k, of the key tiles in 16-byte group g of a
+// mask row (words 4g .. 4g+3: one 128-key tile, or two 64-key tiles),
+// columns >= N cleared.
 template <int D>
-__device__ __forceinline__ void group_live(const uint4& v, int g, int N, LiveBits& bits) {
+__device__ __forceinline__ uint32_t group_live(const uint4& v, int g, int k, int N) {
   const uint32_t x0 = v.x & valid_bits(g * 4, N), x1 = v.y & valid_bits(g * 4 + 1, N);
   const uint32_t x2 = v.z & valid_bits(g * 4 + 2, N), x3 = v.w & valid_bits(g * 4 + 3, N);
   if constexpr (ChainCfg<D>::kWords == 4) {
-    set_live(g, x0 | x1 | x2 | x3, bits);
+    return ((x0 | x1 | x2 | x3) != 0u ? 1u : 0u) << (g - 32 * k);
   } else {
-    set_live(2 * g, x0 | x1, bits);
-    set_live(2 * g + 1, x2 | x3, bits);
+    const int t = 2 * g - 32 * k;
+    return (((x0 | x1) != 0u ? 1u : 0u) << t) | (((x2 | x3) != 0u ? 1u : 0u) << (t + 1));
   }
 }
 
@@ -268,7 +260,20 @@ struct Cursor {
   int i;       // item index (-1 before the first item, n_items when exhausted)
   uint32_t t;  // live tile within the item
   uint32_t n;  // live tiles of item i
+  int w;       // bit word of the current tile
+  uint32_t x;  // live bits of word w above the current tile
+  int kt;      // current key tile
 };
+
+// Steps (w, x) to the next set bit of a slot's live bitset and returns its
+// tile index.  The caller knows such a bit exists (it counts tiles against
+// n_live).
+__device__ __forceinline__ int next_live(const uint32_t* bits, int& w, uint32_t& x) {
+  while (x == 0u) x = bits[++w];
+  const int b = __ffs(x) - 1;
+  x &= x - 1u;
+  return w * 32 + b;
+}
 
 template <int D, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -282,6 +287,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   using C = ChainCfg<D>;
   constexpr int kBN = C::kBN;
   constexpr int kWords = C::kWords;
+  constexpr int kGroupsPerWord = C::kGroupsPerWord;
   constexpr int kSCol = C::kSCol, kPCol = C::kPCol, kOCol = C::kOCol;
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t base = smem_u32(smem);
@@ -335,6 +341,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(smem_u32(&cc.pv_done), 1);
       mbar_init(smem_u32(&cc.drain), 1);
     }
+    for (int c = 0; c < 2; ++c)
+      for (int sl = 0; sl < kSlots; ++sl)
+        for (int k = 0; k < kLiveWords; ++k) ctl.ch[c].scan_bits[sl][k] = 0u;
     ctl.abort_flag = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
@@ -362,6 +371,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto advance = [&](ChainCtl& cc, Cursor& cu, int n_items, bool release) -> int {
     if (cu.i >= 0 && cu.i < n_items && cu.t + 1 < cu.n) {
       ++cu.t;
+      cu.kt = next_live(cc.live_bits[cu.i % kSlots], cu.w, cu.x);
       return 1;
     }
     if (release && cu.i >= 0 && cu.i < n_items) mbar_arrive(smem_u32(&cc.sched_empty[cu.i % kSlots]));
@@ -376,6 +386,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       cu.i = i;
       cu.t = 0;
       cu.n = n;
+      cu.w = 0;
+      cu.x = cc.live_bits[slot][0];
+      cu.kt = next_live(cc.live_bits[slot], cu.w, cu.x);
       return 1;
     }
     cu.i = n_items;
@@ -395,7 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       if constexpr (C::kStageO) tma_prefetch_desc(&tm_o);
-      Cursor kc{-1, 0u, 0u}, vc{-1, 0u, 0u};
+      Cursor kc{-1, 0u, 0u, 0, 0u, 0}, vc{-1, 0u, 0u, 0, 0u, 0};
       uint32_t gk = 0, gv = 0, q_count = 0;  // K, V and Q copies issued
       bool ok = true;
       auto issue_k = [&]() -> bool {
@@ -418,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (gk >= static_cast<uint32_t>(kStages) &&
             !mbar_wait_bounded(smem_u32(&cc.k_empty[stage]), ((gk / kStages) - 1) & 1, abort_flag, timeout_ns))
           return false;
-        const int kt = cc.live[kc.i % kSlots][kc.t];
+        const int kt = kc.kt;
         mbar_arrive_expect_tx(smem_u32(&cc.k_full[stage]), C::kKVBytes);
 #pragma unroll
         for (int dc = 0; dc < C::kDChunks; ++dc)
@@ -433,7 +446,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (gv >= static_cast<uint32_t>(kStages) &&
             !mbar_wait_bounded(smem_u32(&cc.v_empty[stage]), ((gv / kStages) - 1) & 1, abort_flag, timeout_ns))
           return false;
-        const int kt = cc.live[vc.i % kSlots][vc.t];
+        const int kt = vc.kt;
         mbar_arrive_expect_tx(smem_u32(&cc.v_full[stage]), C::kKVBytes);
 #pragma unroll
         for (int dc = 0; dc < C::kDChunks; ++dc)
@@ -490,7 +503,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int n_items = chain_items(c);
       bool ok = true;
 
-      Cursor qc{-1, 0u, 0u};  // next tile to multiply by K^T
+      Cursor qc{-1, 0u, 0u, 0, 0u, 0};  // next tile to multiply by K^T
       uint32_t q_count = 0;
       int qqb = 0;            // Q buffer of the cursor's item
       auto advance_qk = [&]() -> int {
@@ -611,35 +624,42 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (uintptr_t a = a0 & ~static_cast<uintptr_t>(127); a < a1; a += 128)
         asm volatile("prefetch.global.L1 [%0];" ::"l"(a));
     };
-    // Live-tile bits of this thread's row of item j, from the 16-byte groups
-    // at index >= g0 (groups below g0 were OR-ed by the caller).
-    auto scan_rest = [&](const Item& it, int g0, LiveBits& bits) {
-      if (r >= it.rows_valid) return;
+    // ORs this thread's packed-mask row of `it` into live-tile words (bit t of
+    // word k = key tile 32k + t) and adds each warp's words to item j's
+    // scan_bits; the WG barrier after it completes them for the publisher.
+    auto scan_post = [&](const Item& it, int j) {
       const uint32_t* mrow = row_ptr(it);
-      if (vec) {
-        for (int gb = g0; gb < G4; gb += kScanBatch) {
-          uint4 v[kScanBatch];
+      const bool row_ok = r < it.rows_valid;
+      const int nw = (KT + 31) >> 5;
+      for (int k = 0; k < nw; ++k) {
+        uint32_t bits = 0u;
+        if (row_ok) {
+          if (vec) {
+            const int g_lo = k * kGroupsPerWord;
+            const int g_hi = min(G4, g_lo + kGroupsPerWord);
+            for (int gb = g_lo; gb < g_hi; gb += kScanBatch) {
+              uint4 v[kScanBatch];
 #pragma unroll
-          for (int u = 0; u < kScanBatch; ++u)
-            v[u] = (gb + u < G4) ? __ldg(reinterpret_cast<const uint4*>(mrow) + gb + u) : make_uint4(0u, 0u, 0u, 0u);
+              for (int u = 0; u < kScanBatch; ++u)
+                v[u] = (gb + u < g_hi) ? __ldg(reinterpret_cast<const uint4*>(mrow) + gb + u)
+                                       : make_uint4(0u, 0u, 0u, 0u);
 #pragma unroll
-          for (int u = 0; u < kScanBatch; ++u)
-            if (gb + u < G4) group_live<D>(v[u], gb + u, N, bits);
+              for (int u = 0; u < kScanBatch; ++u)
+                if (gb + u < g_hi) bits |= group_live<D>(v[u], gb + u, k, N);
+            }
+          } else {
+            const int w_lo = k * 32 * kWords;
+            const int w_hi = min(W, w_lo + 32 * kWords);
+            for (int cw = w_lo; cw < w_hi; ++cw)
+              if ((__ldg(mrow + cw) & valid_bits(cw, N)) != 0u) bits |= 1u << (cw / kWords - 32 * k);
+          }
         }
-      } else {
-        for (int cw = g0 * 4; cw < W; ++cw) set_live(cw / kWords, __ldg(mrow + cw) & valid_bits(cw, N), bits);
+        const uint32_t x = __reduce_or_sync(0xffffffffu, bits);
+        if (lane == 0 && x != 0u) atomicOr(&cc.scan_bits[j % kSlots][k], x);
       }
     };
-    // Stores this warp's share of item j's live bits (before a WG barrier).
-    auto post_part = [&](int j, const LiveBits& bits) {
-#pragma unroll
-      for (int k = 0; k < kLiveWords; ++k) {
-        const uint32_t x = __reduce_or_sync(0xffffffffu, bits.w[k]);
-        if (lane == 0) cc.part[j % kSlots][wq][k] = x;
-      }
-    };
-    // Warp 0 of the WG, after a WG barrier: builds item j's live list (one
-    // lane per key tile of each 32-tile word, ranks by popcount) and publishes it.
+    // Warp 0 of the WG, after a WG barrier: moves item j's scanned bits (lane
+    // k: word k) into its slot's live bits, counts them and publishes them.
     auto publish = [&](int j) {
       const int slot = j % kSlots;
       if (j >= kSlots && !wait_all(cc.sched_empty[slot], ((j / kSlots) - 1) & 1)) {
@@ -653,19 +673,19 @@ __global__ void __launch_bounds__(kThreads, 1)
         const Item itj = item_of(chain_item(c, j), BH, QT, N, head_major);
         occ_j = occ + 2 * (static_cast<int64_t>(itj.bh) * QT + itj.q0 / kBM);
       }
-      uint32_t n = 0;
-      for (int k = 0; k * 32 < KT; ++k) {
-        uint32_t x;
+      const int nw = (KT + 31) >> 5;  // <= 32: one word per lane
+      uint32_t x = 0u;
+      if (lane < nw) {
         if (occ_j != nullptr) {
-          x = k < 2 ? occ_j[k] : 0u;
+          x = lane < 2 ? occ_j[lane] : 0u;
         } else {
-          x = cc.part[slot][0][k] | cc.part[slot][1][k] | cc.part[slot][2][k] | cc.part[slot][3][k];
+          x = cc.scan_bits[slot][lane];
+          cc.scan_bits[slot][lane] = 0u;  // ready for the item four later
         }
-        if (KT - k * 32 < 32) x &= (1u << (KT - k * 32)) - 1u;
-        if ((x >> lane) & 1u)  // set bits in increasing key-tile order
-          cc.live[slot][n + __popc(x & ((1u << lane) - 1u))] = static_cast<uint16_t>(k * 32 + lane);
-        n += __popc(x);
+        if (KT - lane * 32 < 32) x &= (1u << (KT - lane * 32)) - 1u;
+        cc.live_bits[slot][lane] = x;
       }
+      const uint32_t n = __reduce_add_sync(0xffffffffu, static_cast<uint32_t>(__popc(x)));
       __syncwarp();
       if (lane == 0) {
         cc.n_live[slot] = n;
@@ -679,11 +699,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int n_pre = n_items < 2 ? n_items : 2;
     if (n_pre > 1 && occ == nullptr) prefetch_rows_l1(item_of(chain_item(c, 1), BH, QT, N, head_major));
     for (int j = 0; j < n_pre; ++j) {
-      if (occ == nullptr) {
-        LiveBits bits{};
-        scan_rest(item_of(chain_item(c, j), BH, QT, N, head_major), 0, bits);
-        post_part(j, bits);
-      }
+      if (occ == nullptr) scan_post(item_of(chain_item(c, j), BH, QT, N, head_major), j);
       named_bar_sync(bar_id, 128);
       if (wq == 0) publish(j);
     }
@@ -696,7 +712,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&cc.sched_full[slot]), (i / kSlots) & 1,
                                                               abort_flag, timeout_ns));
       const uint32_t n = ok ? cc.n_live[slot] : 0u;
-      if (n > 0 && !have_mw) fetch_words(it, cc.live[slot][0], mw);
+      // Walk over the item's live bits (word lw, bits above the current tile lx).
+      int lw = 0;
+      uint32_t lx = cc.live_bits[slot][0];
+      const int kt0 = n > 0 ? next_live(cc.live_bits[slot], lw, lx) : 0;
+      if (n > 0 && !have_mw) fetch_words(it, kt0, mw);
       have_mw = false;
       float m_run = -INFINITY, l_run = 0.f, l_out = 0.f;
 
@@ -708,8 +728,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const int slot2 = (i + 1) % kSlots;
           if (__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&cc.sched_full[slot2]), ((i + 1) / kSlots) & 1,
                                                          abort_flag, timeout_ns)) &&
-              cc.n_live[slot2] > 0)
-            next_kt = cc.live[slot2][0];
+              cc.n_live[slot2] > 0) {
+            int w2 = 0;
+            uint32_t x2 = cc.live_bits[slot2][0];
+            next_kt = next_live(cc.live_bits[slot2], w2, x2);
+          }
         }
         if (!wait_all(cc.s_full, g & 1)) {
           ok = false;
@@ -736,7 +759,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         // The next tile's mask words, a whole tile of exponentials ahead of their use.
         if (t + 1 < n) {
-          fetch_words(it, cc.live[slot][t + 1], mw);
+          fetch_words(it, next_live(cc.live_bits[slot], lw, lx), mw);
         } else if (next_kt >= 0) {
           fetch_words(item_of(chain_item(c, i + 1), BH, QT, N, head_major), next_kt, mw);
           have_mw = true;
@@ -840,11 +863,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 16; ++e)
             h[half * 16 + e] = pack2<BF16>(__uint_as_float(u[2 * e]) * inv, __uint_as_float(u[2 * e + 1]) * inv);
         }
-        if (do_scan && occ == nullptr) {
-          LiveBits bits{};
-          scan_rest(itn, 0, bits);
-          post_part(i + 2, bits);
-        }
+        if (do_scan && occ == nullptr) scan_post(itn, i + 2);
         // The previous item's O store must have finished reading the staging tile.
         if (r == 0) bulk_wait_group_read0();
         named_bar_sync(bar_id, 128);
@@ -901,15 +920,16 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         if (lse != nullptr && r < it.rows_valid) lse[static_cast<int64_t>(it.bh) * N + it.q0 + r] = lse_row;
         if (do_scan && occ == nullptr) {
-          LiveBits bits{};
-          if (scan_regs) {
+          if (scan_regs) {  // kEpiGroups groups: tiles 0 .. 15, word 0
+            uint32_t bits = 0u;
 #pragma unroll
             for (int u = 0; u < kEpiGroups; ++u)
-              if (u < G4) group_live<D>(sv[u], u, N, bits);
+              if (u < G4) bits |= group_live<D>(sv[u], u, 0, N);
+            const uint32_t x = __reduce_or_sync(0xffffffffu, bits);
+            if (lane == 0 && x != 0u) atomicOr(&cc.scan_bits[(i + 2) % kSlots][0], x);
           } else {
-            scan_rest(itn, 0, bits);
+            scan_post(itn, i + 2);
           }
-          post_part(i + 2, bits);
         }
         named_bar_sync(bar_id, 128);
         if (wq == 0 && do_scan) publish(i + 2);

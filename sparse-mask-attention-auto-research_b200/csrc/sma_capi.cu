@@ -75,9 +75,8 @@ int attn_fwd_impl(int dtype, const void* q, const void* k, const void* v, const 
     return fail(sma::kErrDtype, "attention: unsupported dtype, need fp16 or bf16");
   if (B < 0 || H < 0 || N < 0 || D <= 0) return fail(sma::kErrArg, "attention: bad dimension");
   if (D != 64 && D != 128) return fail(sma::kErrUnsupportedD, "attention: head dim must be 64 or 128");
-  if (N > SMA_MAX_SEQ_LEN || (D == 128 && N > SMA_MAX_SEQ_LEN_D128))
-    return fail(sma::kErrUnsupportedN,
-                "attention: sequence length above the supported maximum (16384 for head dim 64, 8192 for 128)");
+  if (N > SMA_MAX_SEQ_LEN)
+    return fail(sma::kErrUnsupportedN, "attention: sequence length above the supported maximum (65536)");
   if (occupancy != nullptr && N > SMA_MAX_SEQ_LEN_OCCUPANCY)
     return fail(sma::kErrUnsupportedN, "attention: occupancy map given for a sequence length above 8192");
   if (!(scale > 0.f) || !(scale < INFINITY)) return fail(sma::kErrArg, "attention: scale must be finite and > 0");

@@ -35,12 +35,10 @@ struct AttnParams {
   cudaStream_t stream;
 };
 
-// Largest sequence length per path: the head-dim-64 kernel keeps a live-tile
-// list of up to 128 key tiles per query tile; the head-dim-128 kernel stages a
-// 64-row block of packed mask words (N/32 words a row) in shared memory; the
-// occupancy map holds two 32-bit words (64 key tiles) per query tile.
-constexpr int64_t kMaxSeqLen = 16384;
-constexpr int64_t kMaxSeqLenD128 = 8192;
+// Largest sequence length: the attention kernel keeps one live bit per key
+// tile in 32 words per item (1024 tiles of 64 keys); the occupancy map holds
+// two 32-bit words (64 key tiles of 128) per query tile.
+constexpr int64_t kMaxSeqLen = 65536;
 constexpr int64_t kMaxSeqLenOcc = 8192;
 
 int launch_pack_mask(const uint8_t* mask, uint32_t* packed, int64_t rows, int64_t n,
@@ -74,7 +72,7 @@ cudaError_t launch_pdl(void (*kern)(Params...), unsigned grid, unsigned block, s
 }
 
 // Persistent two-chain kernel (attn_fwd_chain.cu): head dims 64 and 128, N up
-// to 16384 / 8192.  launch_attn_fwd dispatches to it when chain_supported().
+// to kMaxSeqLen.  launch_attn_fwd dispatches to it when chain_supported().
 bool chain_supported(const AttnParams& p);
 int launch_attn_fwd_chain(const AttnParams& p, const char** msg);
 

@@ -24,8 +24,7 @@ SMA_ERR_CUDA = 7
 
 SMA_DTYPE_FP16 = 0
 SMA_DTYPE_BF16 = 1
-SMA_MAX_SEQ_LEN = 16384  # head dim 64
-SMA_MAX_SEQ_LEN_D128 = 8192
+SMA_MAX_SEQ_LEN = 65536
 SMA_MAX_SEQ_LEN_OCCUPANCY = 8192
 
 # Every symbol include/sma_capi.h declares, with (restype, argtypes).

@@ -60,8 +60,8 @@ def test_attn_rejects_head_dim(lib):
 
 def test_attn_rejects_long_sequence(lib):
     assert _attn(lib, N=L.SMA_MAX_SEQ_LEN + 1) == L.SMA_ERR_UNSUPPORTED_N
-    assert _attn(lib, N=L.SMA_MAX_SEQ_LEN_D128 + 1, D=128) == L.SMA_ERR_UNSUPPORTED_N
-    assert b"16384" in lib.sma_last_error()
+    assert _attn(lib, N=L.SMA_MAX_SEQ_LEN + 1, D=128) == L.SMA_ERR_UNSUPPORTED_N
+    assert b"65536" in lib.sma_last_error()
     # The map holds 64 key tiles per query tile: longer sequences are refused with it.
     args = (0, 16, 16, 16, 16, 16, 16, None, 1, 1, L.SMA_MAX_SEQ_LEN_OCCUPANCY + 1, 64, 0.125, None)
     assert lib.sma_attn_fwd_occupancy(*args) == L.SMA_ERR_UNSUPPORTED_N
