@@ -99,7 +99,8 @@ SMA_API int sma_pack_mask_occupancy(const void* mask, void* packed, void* occupa
  * sma_attn_fwd with the occupancy map written by sma_pack_mask_occupancy for
  * the same mask: the head-dim-64 kernel takes its live key tiles from the
  * map instead of scanning the packed rows; results are identical to
- * sma_attn_fwd.  (Head dim 128 stages the packed rows anyway and ignores it.)
+ * sma_attn_fwd.  (The map describes 128-key tiles; head dim 128 works on
+ * 64-key tiles, scans the packed rows and ignores it.)
  * No reference counterpart.
  */
 SMA_API int sma_attn_fwd_occupancy(int dtype, const void* q, const void* k, const void* v, const void* mask_packed,
