@@ -20,6 +20,9 @@ Functions
                                   CUDA path's -FLT_MAX for rows with no set bit
                                   (csrc/sparse_attention.cu:139-142)
   attention_parallel(...)         the same, split over heads on a thread pool
+  attention_backward(q, k, v, mask, scale, dout)
+                                  python/sparse_attention.py:97-111 (the
+                                  reference's CPU backward formulas)
 """
 
 import concurrent.futures
@@ -112,6 +115,32 @@ def lse(q, k, mask, scale):
     m0 = np.where(empty, np.float32(0), m)
     out = m0 + np.log(np.exp(s - m0[..., None]).sum(axis=-1))
     return np.where(empty, -FLT_MAX, out).astype(np.float32)
+
+
+def attention_backward(q, k, v, mask, scale, dout):
+    """FP32 gradients (dq, dk, dv) of attention() for the upstream gradient
+    `dout`, with the reference's CPU backward formulas
+    (python/sparse_attention.py:97-111): P = softmax of the masked scaled
+    scores (0 on rows with no kept key); dv = P^T dout; dP = dout v^T, 0 where
+    masked; dS = P * (dP - rowsum(dP * P)) * scale; dq = dS k; dk = dS^T q."""
+    q = np.asarray(q, dtype=np.float32)
+    k = np.asarray(k, dtype=np.float32)
+    v = np.asarray(v, dtype=np.float32)
+    dout = np.asarray(dout, dtype=np.float32)
+    mask = np.asarray(mask).astype(bool)
+    s = np.where(mask, _scores(q, k, scale), np.float32(-np.inf))
+    m = s.max(axis=-1, keepdims=True)
+    empty = ~np.isfinite(m)
+    m = np.where(empty, np.float32(0), m)
+    e = np.exp(s - m)
+    denom = e.sum(axis=-1, keepdims=True)
+    p = np.where(empty, np.float32(0), e / np.where(empty, np.float32(1), denom)).astype(np.float32)
+    dv = np.matmul(np.swapaxes(p, -1, -2), dout)
+    dp = np.where(mask, np.matmul(dout, np.swapaxes(v, -1, -2)), np.float32(0))
+    ds = p * (dp - (dp * p).sum(axis=-1, keepdims=True)) * np.float32(scale)
+    dq = np.matmul(ds, k)
+    dk = np.matmul(np.swapaxes(ds, -1, -2), q)
+    return dq.astype(np.float32), dk.astype(np.float32), dv.astype(np.float32)
 
 
 def _flat(x):

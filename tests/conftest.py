@@ -58,7 +58,9 @@ def load_golden(path):
     meta = json.loads(str(z["meta"]))
     n = int(z["n"])
     mask = np.unpackbits(z["mask"], axis=-1, bitorder="little")[..., :n].astype(bool)
-    case = dict(meta=meta, mask=torch.from_numpy(mask), packed=torch.from_numpy(z["packed"]))
+    case = dict(meta=meta, mask=torch.from_numpy(mask))
+    if "packed" in z:
+        case["packed"] = torch.from_numpy(z["packed"])
     if meta["kind"] == "attention":
         dtype = getattr(torch, meta["dtype"])
         case.update(
@@ -67,6 +69,19 @@ def load_golden(path):
             v=_from_bits(z["v"], dtype),
             out=torch.from_numpy(z["out"]),
             lse=torch.from_numpy(z["lse"]),
+            dtype=dtype,
+        )
+    elif meta["kind"] == "backward":
+        dtype = getattr(torch, meta["dtype"])
+        case.update(
+            q=_from_bits(z["q"], dtype),
+            k=_from_bits(z["k"], dtype),
+            v=_from_bits(z["v"], dtype),
+            dout=_from_bits(z["dout"], dtype),
+            lse=torch.from_numpy(z["lse"]),
+            dq=torch.from_numpy(z["dq"]),
+            dk=torch.from_numpy(z["dk"]),
+            dv=torch.from_numpy(z["dv"]),
             dtype=dtype,
         )
     return case

@@ -11,6 +11,8 @@ takes its CPU paths:
   sparse_attention_ref()          python/sparse_attention.py:26-44   (FP32 oracle, as run.py:435)
   SparseAttentionFunction.forward python/sparse_attention.py:52-80   (fallback LSE, :67-76)
   generate_random_sparse_mask()   python/sparse_attention.py:209-239 (the reference's own masks)
+  SparseAttentionFunction.backward python/sparse_attention.py:82-114 (its CPU formulas; run on FP32
+                                  copies of the fp16/bf16 inputs so the gradients stay in FP32)
 
 Each case is one .npz: q/k/v as raw 16-bit patterns plus their dtype name,
 the bool mask bit-packed with numpy (little bit order), the reference's FP32
@@ -61,6 +63,30 @@ def attention_case(ref, name, q, k, v, mask, seed, note):
           out=out.numpy().astype(np.float32), lse=lse.numpy().astype(np.float32),
           packed=packed.numpy().astype(np.int32), meta=json.dumps(meta))
     print(f"{name}: {meta['shape']} {meta['dtype']} density={mask.float().mean().item():.4f}")
+
+
+def backward_case(ref, name, q, k, v, mask, dout, seed, note):
+    """The reference's backward formulas (python/sparse_attention.py:97-111)
+    on FP32 copies of the 16-bit inputs, so dq/dk/dv are its FP32 results."""
+    B, H, N, D = q.shape
+    scale = 1.0 / math.sqrt(D)
+    qf, kf, vf, dof = q.float(), k.float(), v.float(), dout.float()
+    packed = ref.pack_mask(mask)
+    ctx = _Ctx()
+    ref.SparseAttentionFunction.forward(ctx, qf, kf, vf, packed, mask, scale, N)
+    lse = ctx.saved[4]
+    ctx.saved_tensors = ctx.saved
+    ctx.scale = scale
+    dq, dk, dv = ref.SparseAttentionFunction.backward(ctx, dof)[:3]
+    meta = dict(kind="backward", name=name, shape=[B, H, N, D], dtype=str(q.dtype).replace("torch.", ""),
+                seed=seed, scale=scale, note=note,
+                reference=["python/sparse_attention.py:82-114", "python/sparse_attention.py:26-44",
+                           "python/sparse_attention.py:67-76"])
+    _save(name, q=_bits16(q), k=_bits16(k), v=_bits16(v), dout=_bits16(dout),
+          mask=np.packbits(mask.numpy(), axis=-1, bitorder="little"), n=np.int64(N),
+          lse=lse.numpy().astype(np.float32), dq=dq.numpy().astype(np.float32),
+          dk=dk.numpy().astype(np.float32), dv=dv.numpy().astype(np.float32), meta=json.dumps(meta))
+    print(f"{name}: {meta['shape']} {meta['dtype']} backward density={mask.float().mean().item():.4f}")
 
 
 def pack_case(ref, name, mask, seed, note):
@@ -187,6 +213,38 @@ def main():
 
     for name, q, k, v, m, seed, note in cases:
         attention_case(ref, name, q, k, v, m, seed, note)
+
+    # ---------------------------------------------------------------- backward cases
+    bcases = []
+    gen = torch.Generator().manual_seed(201)
+    q, k, v = qkv(gen, 1, 2, 512, 64, torch.float16)
+    bcases.append(("bwd_c1_mini", q, k, v, bern(gen, 1, 2, 512, 0.25), 201, "c1 recipe, B1 H2"))
+    gen = torch.Generator().manual_seed(202)
+    q, k, v = qkv(gen, 2, 1, 100, 64, torch.float16)
+    m = bern(gen, 2, 1, 100, 0.3)
+    m[1, 0, 7, :] = False
+    bcases.append(("bwd_N100_fp16", q, k, v, m, 202, "N=100 (partial tiles), one fully masked row"))
+    gen = torch.Generator().manual_seed(203)
+    q, k, v = qkv(gen, 1, 2, 256, 64, torch.bfloat16)
+    bcases.append(("bwd_N256_bf16", q, k, v, bern(gen, 1, 2, 256, 0.25), 203, "bf16"))
+    gen = torch.Generator().manual_seed(204)
+    q, k, v = qkv(gen, 1, 1, 1024, 64, torch.float16)
+    i = torch.arange(1024)
+    m = (i[None, :] <= i[:, None]) & (torch.rand(1, 1, 1024, 1024, generator=gen) < 0.5)
+    m |= torch.eye(1024, dtype=torch.bool)
+    bcases.append(("bwd_c4_mini", q, k, v, m, 204, "c4 recipe (causal): dead blocks above the diagonal"))
+    gen = torch.Generator().manual_seed(205)
+    q, k, v = qkv(gen, 1, 1, 512, 64, torch.float16, mult=4.0)
+    m = torch.zeros(1, 1, 512, 512, dtype=torch.bool)
+    m[0, 0, 128:384, 256:448] = torch.rand(256, 192, generator=gen) < 0.4
+    bcases.append(("bwd_block_N512", q, k, v, m, 205, "live block only; larger scores; zero rows and columns"))
+    gen = torch.Generator().manual_seed(206)
+    q, k, v = qkv(gen, 1, 1, 200, 128, torch.bfloat16)
+    bcases.append(("bwd_N200_bf16_D128", q, k, v, bern(gen, 1, 1, 200, 0.3), 206, "D=128 (oracle only)"))
+    for name, q, k, v, m, seed, note in bcases:
+        g2 = torch.Generator().manual_seed(seed + 1000)
+        dout = torch.randn(q.shape, generator=g2).to(q.dtype)
+        backward_case(ref, name, q, k, v, m, dout, seed, note)
 
 
 if __name__ == "__main__":

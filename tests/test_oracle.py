@@ -93,3 +93,27 @@ def test_occupancy_matches_reference_packed_bits(path):
         for r in range(qt):
             live = (cols[:, :, 128 * r:128 * (r + 1)] != 0).any(axis=(2, 3))
             assert np.array_equal((occ[:, :, r, t // 32] >> (t % 32)) & 1, live.astype(np.uint32))
+
+
+@pytest.mark.parametrize("path", golden_paths("bwd"), ids=golden_ids("bwd"))
+def test_backward_vs_reference(path):
+    """The oracle's backward against the reference's own CPU backward
+    (python/sparse_attention.py:97-111) on the same inputs."""
+    case = load_golden(path)
+    scale = case["meta"]["scale"]
+    q, k, v, dout, m = (case[x].float().numpy() for x in ("q", "k", "v", "dout", "mask"))
+    dq, dk, dv = oracle.attention_backward(q, k, v, m, scale, dout)
+    for got, name in ((dq, "dq"), (dk, "dk"), (dv, "dv")):
+        want = case[name].numpy()
+        np.testing.assert_allclose(got, want, atol=1e-4 * max(1.0, np.abs(want).max()), rtol=1e-4, err_msg=name)
+    empty = ~case["mask"].numpy().any(axis=-1)
+    assert np.all(dq[empty] == 0), "rows with no kept key get no gradient"
+
+
+def test_backward_planted_error_is_caught():
+    case = load_golden(golden_path("bwd_c1_mini"))
+    m = case["mask"].numpy().copy()
+    m[0, 1, 20, np.argmax(m[0, 1, 20])] = False  # drop one kept key
+    q, k, v, dout = (case[x].float().numpy() for x in ("q", "k", "v", "dout"))
+    dq, dk, dv = oracle.attention_backward(q, k, v, m, case["meta"]["scale"], dout)
+    assert np.abs(dq - case["dq"].numpy()).max() > 1e-3
