@@ -108,6 +108,26 @@ SMA_API int sma_attn_fwd_occupancy(int dtype, const void* q, const void* k, cons
                                    int64_t D, float scale, void* stream);
 
 /*
+ * Masked-softmax attention backward for head dim 64: given the forward's
+ * inputs, its out and lse (as written by sma_attn_fwd with a non-NULL lse)
+ * and the upstream gradient dout, writes dq, dk, dv ([B, H, N, D] of `dtype`):
+ *   P = exp(scale * q k^T - lse) where the mask bit is set, else 0
+ *   dv = P^T dout;  dS = P * (dout v^T - rowsum(dout * out));
+ *   dq = scale * dS k;  dk = scale * dS^T q
+ * dq_accum (FP32 [B, H, N, D]) and delta (FP32 [B, H, N]) are caller-provided
+ * scratch.  Rows with no set bit get dq = 0; keys no row attends get dk = dv = 0.
+ * Needs D = 64, 16-byte aligned q/k/v/out/dout/dq/dk/dv/dq_accum.
+ *
+ * Replaces: sparse_attn_cuda.backward(dout, q, k, v, out, lse, mask_packed,
+ *           dq, dk, dv, scale), called by python/sparse_attention.py:93-96 but
+ *           never bound by csrc/binding.cpp; the result follows the
+ *           reference's CPU formulas (python/sparse_attention.py:97-111).
+ */
+SMA_API int sma_attn_bwd(int dtype, const void* q, const void* k, const void* v, const void* out, const void* dout,
+                         const float* lse, const void* mask_packed, void* dq, void* dk, void* dv, float* dq_accum,
+                         float* delta, int64_t B, int64_t H, int64_t N, int64_t D, float scale, void* stream);
+
+/*
  * Synchronise `stream`, then report whether any kernel of this library on the
  * current device gave up a bounded device-side wait since the last clear
  * (SMA_ERR_TIMEOUT), or whether the stream holds a CUDA error (SMA_ERR_CUDA).

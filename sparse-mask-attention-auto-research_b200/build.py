@@ -23,7 +23,7 @@ INCLUDE = os.path.join(REPO, "include")
 BUILD_DIR = os.path.join(HERE, "_build")
 LIB_PATH = os.path.join(HERE, "libsma.so")
 
-SOURCES = ["sma_capi.cu", "pack_mask.cu", "attn_fwd.cu", "attn_fwd_chain.cu"]
+SOURCES = ["sma_capi.cu", "pack_mask.cu", "attn_fwd.cu", "attn_fwd_chain.cu", "tma_map.cu", "attn_bwd.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON_FLAGS = [
     "-O3",

@@ -1,0 +1,545 @@
+// Fused masked-softmax attention backward, head dim 64 (sm_100a).
+//
+// The reference binds no CUDA backward (python/sparse_attention.py:93-96 calls
+// sparse_attn_cuda.backward, which csrc/binding.cpp never defines); its CPU
+// formulas (python/sparse_attention.py:97-111) define the result:
+//   P   = softmax of the masked scaled scores, rebuilt here from the forward's
+//         LSE: P_ij = bit(i,j) ? exp(scale * q_i.k_j - lse_i) : 0
+//   dV  = P^T dO
+//   dP  = dO V^T (0 where masked; P is 0 there, so dS is too)
+//   dS  = P * (dP - Delta),  Delta_i = sum_d dO_id O_id  (= rowsum(P * dP))
+//   dQ  = scale * dS K,   dK = scale * dS^T Q
+//
+// Kernels (one stream, in order):
+//   bwd_delta_kernel   Delta from dO and O (FP32), 8 threads per row
+//   attn_bwd_kernel    one CTA per (batch*head, 128-key tile).  K and V stay
+//                      in shared memory, dK and dV accumulate in TMEM, and the
+//                      CTA walks the 128-row query tiles whose mask block with
+//                      its key tile has a set bit.  Per live query tile:
+//                        MMA  S^T = K Q^T, dP^T = V dO^T   (M = keys)
+//                        P^T, dS^T in registers (thread t = key t), written
+//                        back to TMEM (fp16/bf16) and dS to shared memory
+//                        MMA  dV += P^T dO, dK += dS^T Q  (A from TMEM)
+//                             dQ_part = dS K              (A from shared memory, M-major)
+//                        dQ_part * scale is added into an FP32 accumulator in
+//                        global memory (red.global.add.v4.f32)
+//   bwd_dq_convert_kernel  FP32 accumulator -> dq in the input dtype
+//
+// Warps (192 threads): 0-3 compute (thread t <-> TMEM lane t), 4 loader
+// (TMA of K, V, Q, dO; mask words, LSE and Delta of the query tile staged in
+// shared memory), 5 MMA issuer and TMEM owner.
+// TMEM (512 columns): S^T [0,128) (P^T over its first 64), dP^T [128,256)
+// (dS^T over its first 64), dV [256,320), dK [320,384), dQ_part [384,448).
+// Every wait is bounded and reports through the device error word.
+#include <cfloat>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "sma_internal.h"
+#include "sma_ptx.cuh"
+
+namespace sma {
+namespace {
+
+constexpr int kD = 64;
+constexpr int kT = 128;  // query rows and keys per tile
+constexpr int kThreads = 192;
+constexpr int kTileBytes = kT * kD * 2;  // 16 KiB
+constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 320, kColDQ = 384;
+constexpr int kTmemCols = 512;
+constexpr float kLog2e = 1.44269504088896340736f;
+constexpr int kMaxDevices = 64;
+
+struct BwdCtl {
+  uint64_t kv_full;    // K and V landed
+  uint64_t ld_full;    // query tile staged (Q, dO by TMA; mask, LSE, Delta by the loader warp)
+  uint64_t st_full;    // S^T and dP^T complete
+  uint64_t p_full;     // P^T, dS^T in TMEM and dS in shared memory (4 compute warps)
+  uint64_t dq_full;    // dV, dK, dQ_part MMAs complete
+  uint64_t tile_free;  // compute warps and MMA issuer done with the query tile (5 arrivals)
+  uint64_t drain;
+  uint32_t tmem_base;
+  uint32_t live;
+  uint32_t abort_flag;
+};
+
+// Shared memory: K | V | Q | dO (16 KiB each, 128-byte swizzle) | dS (two
+// 16 KiB M-major chunks of 64 queries) | mask words [4][128] | lse2 [128] |
+// Delta [128] | control.
+constexpr int kOffK = 0, kOffV = kTileBytes, kOffQ = 2 * kTileBytes, kOffDO = 3 * kTileBytes;
+constexpr int kOffDS = 4 * kTileBytes;
+constexpr int kOffMask = kOffDS + 2 * kTileBytes;
+constexpr int kOffLse = kOffMask + 4 * kT * 4;
+constexpr int kOffDelta = kOffLse + kT * 4;
+constexpr int kOffCtl = kOffDelta + kT * 4;
+// Above half of the SM's shared memory, so one CTA holds an SM (its TMEM
+// allocation takes all 512 columns).
+constexpr size_t kSmemBytes = 120 * 1024;
+static_assert(kOffCtl + sizeof(BwdCtl) <= kSmemBytes, "shared memory layout");
+
+__device__ __forceinline__ float ex2f(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <bool BF16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+  if constexpr (BF16) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  } else {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+}
+
+template <bool BF16>
+__device__ __forceinline__ float2 unpack2(uint32_t x) {
+  if constexpr (BF16) {
+    return __bfloat1622float2(*reinterpret_cast<__nv_bfloat162*>(&x));
+  } else {
+    return __half22float2(*reinterpret_cast<__half2*>(&x));
+  }
+}
+
+__device__ __forceinline__ void red_add_v4(float* dst, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+// Bits of packed-mask word cw of a row that address columns < N.
+__device__ __forceinline__ uint32_t valid_bits(int cw, int N) {
+  const int valid = N - cw * 32;
+  return valid >= 32 ? 0xFFFFFFFFu : (valid <= 0 ? 0u : ((1u << valid) - 1u));
+}
+
+// Delta[row] = sum_d dO[row, d] * O[row, d] in FP32; 8 threads per row, one
+// 16-byte load of each operand per thread.
+template <bool BF16>
+__global__ void __launch_bounds__(256) bwd_delta_kernel(const uint4* __restrict__ dout, const uint4* __restrict__ out,
+                                                         float* __restrict__ delta, int64_t rows) {
+  const int64_t gid = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  const int64_t row = gid >> 3;
+  float acc = 0.f;
+  if (row < rows) {
+    const uint4 a = __ldg(dout + gid), b = __ldg(out + gid);
+    const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 x = unpack2<BF16>(aw[e]), y = unpack2<BF16>(bw[e]);
+      acc = fmaf(x.x, y.x, acc);
+      acc = fmaf(x.y, y.y, acc);
+    }
+  }
+  acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+  acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+  acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+  if (row < rows && (threadIdx.x & 7) == 0) delta[row] = acc;
+}
+
+// dq[i] = acc[i] in the input dtype, 8 elements per thread.
+template <bool BF16>
+__global__ void __launch_bounds__(256) bwd_dq_convert_kernel(const float4* __restrict__ acc, uint4* __restrict__ dq,
+                                                              int64_t n8) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
+  if (i >= n8) return;
+  const float4 a = acc[2 * i], b = acc[2 * i + 1];
+  dq[i] = make_uint4(pack2<BF16>(a.x, a.y), pack2<BF16>(a.z, a.w), pack2<BF16>(b.x, b.y), pack2<BF16>(b.z, b.w));
+}
+
+template <bool BF16>
+__global__ void __launch_bounds__(kThreads, 1)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                    const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
+                    const uint32_t* __restrict__ mask, const float* __restrict__ lse,
+                    const float* __restrict__ delta, float* __restrict__ dq_acc, uint16_t* __restrict__ dk,
+                    uint16_t* __restrict__ dv, int N, int W, int KT, int QT, int vec, float scale,
+                    uint32_t* err_word, uint64_t timeout_ns) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const uint32_t base = smem_u32(smem);
+  if ((base & 1023u) != 0u) {
+    if (threadIdx.x == 0) atomicOr(err_word, kDevErrLayout);
+    return;
+  }
+  BwdCtl& ctl = *reinterpret_cast<BwdCtl*>(smem + kOffCtl);
+  uint32_t* s_mask = reinterpret_cast<uint32_t*>(smem + kOffMask);  // word w of query row i at [w * kT + i]
+  float* s_lse = reinterpret_cast<float*>(smem + kOffLse);          // LSE * log2(e) per query row
+  float* s_delta = reinterpret_cast<float*>(smem + kOffDelta);
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int bh = static_cast<int>(blockIdx.x) / KT;
+  const int kt = static_cast<int>(blockIdx.x) - bh * KT;
+  const int k0 = kt * kT;
+  volatile uint32_t* abort_flag = &ctl.abort_flag;
+
+  if (threadIdx.x == 128) {
+    mbar_init(smem_u32(&ctl.kv_full), 1);
+    mbar_init(smem_u32(&ctl.ld_full), 1);
+    mbar_init(smem_u32(&ctl.st_full), 1);
+    mbar_init(smem_u32(&ctl.p_full), 4);
+    mbar_init(smem_u32(&ctl.dq_full), 1);
+    mbar_init(smem_u32(&ctl.tile_free), 5);  // 4 compute warps + the MMA issuer
+    mbar_init(smem_u32(&ctl.drain), 1);
+    ctl.abort_flag = 0;
+    ctl.live = 0;
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 5) {
+    tmem_alloc(smem_u32(&ctl.tmem_base), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl.tmem_base;
+  pdl_wait_prior_grid();
+
+  auto fail = [&]() {
+    ctl.abort_flag = 1;
+    atomicOr(err_word, kDevErrTimeout);
+  };
+
+  if (warp == 4) {
+    // ================================================================ loader
+    if (lane == 0) {
+      tma_prefetch_desc(&tm_q);
+      tma_prefetch_desc(&tm_k);
+      tma_prefetch_desc(&tm_v);
+      tma_prefetch_desc(&tm_do);
+      mbar_arrive_expect_tx(smem_u32(&ctl.kv_full), 2 * kTileBytes);
+      tma_load_3d(base + kOffK, &tm_k, smem_u32(&ctl.kv_full), 0, k0, bh);
+      tma_load_3d(base + kOffV, &tm_v, smem_u32(&ctl.kv_full), 0, k0, bh);
+    }
+    bool ok = true;
+    int last_copy = -1;  // last query tile whose Q/dO copies were started
+    for (int qi = 0; qi < QT; ++qi) {
+      // The previous query tile's staging is free once the compute warps and
+      // the MMA issuer are done with it (its MMAs have completed by then).
+      if (qi > 0 &&
+          !__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&ctl.tile_free), (qi - 1) & 1, abort_flag, timeout_ns))) {
+        ok = false;
+        break;
+      }
+      const int i0 = qi * kT;
+      uint32_t any = 0u;
+#pragma unroll
+      for (int rr = 0; rr < 4; ++rr) {
+        const int i = lane + 32 * rr;
+        const int row = i0 + i;
+        uint32_t w4[4] = {0u, 0u, 0u, 0u};
+        float l2 = 0.f, de = 0.f;
+        if (row < N) {
+          const uint32_t* mrow = mask + (static_cast<int64_t>(bh) * N + row) * W + kt * 4;
+          if (vec) {
+            const uint4 x = __ldg(reinterpret_cast<const uint4*>(mrow));
+            w4[0] = x.x;
+            w4[1] = x.y;
+            w4[2] = x.z;
+            w4[3] = x.w;
+          } else {
+#pragma unroll
+            for (int w = 0; w < 4; ++w) w4[w] = (kt * 4 + w < W) ? __ldg(mrow + w) : 0u;
+          }
+#pragma unroll
+          for (int w = 0; w < 4; ++w) w4[w] &= valid_bits(kt * 4 + w, N);
+          // -FLT_MAX (a row with no kept key) becomes -inf; such a row has no
+          // mask bit, so its P is 0 by the select and never uses this value.
+          l2 = lse[static_cast<int64_t>(bh) * N + row] * kLog2e;
+          de = delta[static_cast<int64_t>(bh) * N + row];
+        }
+#pragma unroll
+        for (int w = 0; w < 4; ++w) {
+          s_mask[w * kT + i] = w4[w];
+          any |= w4[w];
+        }
+        s_lse[i] = l2;
+        s_delta[i] = de;
+      }
+      const bool live = __any_sync(0xffffffffu, any != 0u);
+      __syncwarp();
+      if (lane == 0) {
+        ctl.live = live ? 1u : 0u;
+        if (live) {
+          mbar_arrive_expect_tx(smem_u32(&ctl.ld_full), 2 * kTileBytes);
+          tma_load_3d(base + kOffQ, &tm_q, smem_u32(&ctl.ld_full), 0, i0, bh);
+          tma_load_3d(base + kOffDO, &tm_do, smem_u32(&ctl.ld_full), 0, i0, bh);
+          last_copy = qi;
+        } else {
+          mbar_arrive(smem_u32(&ctl.ld_full));
+        }
+      }
+    }
+    if (!ok && lane == 0) {
+      fail();
+      // Let the copies this warp started land before the CTA exits.
+      uint32_t zero = 0;
+      mbar_wait_bounded(smem_u32(&ctl.kv_full), 0, &zero, timeout_ns);
+      if (last_copy >= 0) mbar_wait_bounded(smem_u32(&ctl.ld_full), last_copy & 1, &zero, timeout_ns);
+    }
+  } else if (warp == 5) {
+    // ================================================================ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = make_idesc_f16(kT, kT, BF16 ? 1 : 0, 0);       // S^T, dP^T (M = keys)
+      constexpr uint32_t idesc_kv = make_idesc_f16(kT, kD, BF16 ? 1 : 0, 1);      // dV, dK (B M/N-major)
+      constexpr uint32_t idesc_q = make_idesc_f16(kT, kD, BF16 ? 1 : 0, 1, 1);    // dQ (A and B M/N-major)
+      const uint32_t sK = base + kOffK, sV = base + kOffV, sQ = base + kOffQ, sDO = base + kOffDO;
+      const uint32_t sDS = base + kOffDS;
+      bool ok = mbar_wait_bounded(smem_u32(&ctl.kv_full), 0, abort_flag, timeout_ns);
+      uint32_t lt = 0;  // live query tiles done
+      for (int qi = 0; ok && qi < QT; ++qi) {
+        if (!mbar_wait_bounded(smem_u32(&ctl.ld_full), qi & 1, abort_flag, timeout_ns) ||
+            (qi > 0 && !mbar_wait_bounded(smem_u32(&ctl.tile_free), (qi - 1) & 1, abort_flag, timeout_ns))) {
+          ok = false;
+          break;
+        }
+        if (ctl.live != 0u) {
+          tc_fence_after();
+#pragma unroll
+          for (int kk = 0; kk < kD / 16; ++kk)
+            mma_ss(tmem + kColS, smem_desc_sw128(sK + kk * 32, 16, 1024), smem_desc_sw128(sQ + kk * 32, 16, 1024),
+                   idesc_s, kk > 0 ? 1u : 0u);
+#pragma unroll
+          for (int kk = 0; kk < kD / 16; ++kk)
+            mma_ss(tmem + kColDP, smem_desc_sw128(sV + kk * 32, 16, 1024),
+                   smem_desc_sw128(sDO + kk * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+          mma_commit(smem_u32(&ctl.st_full));
+          if (!mbar_wait_bounded(smem_u32(&ctl.p_full), lt & 1, abort_flag, timeout_ns)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // 16 query rows per step: 8 packed TMEM columns of P^T / dS^T, 2048
+          // bytes (16 rows of 128) into the M/N-major shared-memory operands.
+#pragma unroll
+          for (int kk = 0; kk < kT / 16; ++kk)
+            mma_ts(tmem + kColDV, tmem + kColS + kk * 8, smem_desc_sw128(sDO + kk * 2048, kT * 128, 1024),
+                   idesc_kv, (lt > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+          for (int kk = 0; kk < kT / 16; ++kk)
+            mma_ts(tmem + kColDK, tmem + kColDP + kk * 8, smem_desc_sw128(sQ + kk * 2048, kT * 128, 1024),
+                   idesc_kv, (lt > 0 || kk > 0) ? 1u : 0u);
+          // dQ_part = dS K: 16 keys per step; dS's two 64-query chunks are
+          // kT * 128 bytes apart.
+#pragma unroll
+          for (int kk = 0; kk < kT / 16; ++kk)
+            mma_ss(tmem + kColDQ, smem_desc_sw128(sDS + kk * 2048, kT * 128, 1024),
+                   smem_desc_sw128(sK + kk * 2048, kT * 128, 1024), idesc_q, kk > 0 ? 1u : 0u);
+          mma_commit(smem_u32(&ctl.dq_full));
+          ++lt;
+        }
+        mbar_arrive(smem_u32(&ctl.tile_free));
+      }
+      if (!ok) fail();
+      // Every MMA this thread issued must complete before TMEM is released.
+      mma_commit(smem_u32(&ctl.drain));
+      uint32_t zero = 0;
+      mbar_wait_bounded(smem_u32(&ctl.drain), 0, &zero, timeout_ns);
+    }
+  } else {
+    // ================================================================ compute
+    const int t = threadIdx.x;  // key row of the tile for P^T / dS^T / dK / dV, query row for dQ_part
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
+    const float c2 = scale * kLog2e;
+    const uint32_t* my_words = s_mask + (t >> 5) * kT;  // the word holding this key, for each query row
+    const int kb = t & 31;
+    bool ok = true;
+    uint32_t lt = 0;
+    auto wait_all = [&](uint64_t& bar, uint32_t parity) -> bool {
+      const bool all =
+          __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&bar), parity, abort_flag, timeout_ns));
+      tc_fence_after();
+      return all;
+    };
+    auto arrive_warp = [&](uint64_t& bar) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bar));
+    };
+    for (int qi = 0; qi < QT; ++qi) {
+      if (ok) ok = wait_all(ctl.ld_full, qi & 1);
+      if (ok && ctl.live != 0u) {
+        ok = wait_all(ctl.st_full, lt & 1);
+        if (ok) {
+#pragma unroll 1
+          for (int c = 0; c < kT / 32; ++c) {
+            float s[32], dp[32];
+            tmem_ld32f(t_lane + kColS + c * 32, s);
+            tmem_ld32f(t_lane + kColDP + c * 32, dp);
+            tmem_wait_ld();
+            uint32_t pw[16], dw[16];
+#pragma unroll
+            for (int e = 0; e < 32; e += 4) {
+              const uint4 m4 = *reinterpret_cast<const uint4*>(my_words + c * 32 + e);
+              const float4 l4 = *reinterpret_cast<const float4*>(s_lse + c * 32 + e);
+              const float4 d4 = *reinterpret_cast<const float4*>(s_delta + c * 32 + e);
+              const uint32_t mm[4] = {m4.x, m4.y, m4.z, m4.w};
+              const float ll[4] = {l4.x, l4.y, l4.z, l4.w}, dd[4] = {d4.x, d4.y, d4.z, d4.w};
+              float p[4], ds[4];
+#pragma unroll
+              for (int u = 0; u < 4; ++u) {
+                p[u] = ((mm[u] >> kb) & 1u) ? ex2f(fmaf(s[e + u], c2, -ll[u])) : 0.f;
+                ds[u] = p[u] * (dp[e + u] - dd[u]);
+              }
+              pw[e / 2] = pack2<BF16>(p[0], p[1]);
+              pw[e / 2 + 1] = pack2<BF16>(p[2], p[3]);
+              dw[e / 2] = pack2<BF16>(ds[0], ds[1]);
+              dw[e / 2 + 1] = pack2<BF16>(ds[2], ds[3]);
+            }
+            // P^T and dS^T over the S^T / dP^T columns already read (chunk c
+            // writes columns 16c.., whose values belong to chunks <= c).
+            tmem_st16(t_lane + kColS + c * 16, pw);
+            tmem_st16(t_lane + kColDP + c * 16, dw);
+            // dS for the dQ MMA: row t of the M-major operand, queries
+            // 32c .. 32c+31 = 16-byte chunks 4(c&1) .. +3 of 64-query chunk c/2,
+            // 128-byte swizzle (chunk index XOR row % 8).
+            uint8_t* drow = smem + kOffDS + (c >> 1) * kTileBytes + t * 128;
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              *reinterpret_cast<uint4*>(drow + ((((c & 1) * 4 + j) ^ (t & 7)) * 16)) =
+                  make_uint4(dw[4 * j], dw[4 * j + 1], dw[4 * j + 2], dw[4 * j + 3]);
+          }
+          tmem_wait_st();
+          fence_proxy_async_smem();  // dS written by this thread, read by the tensor core
+          arrive_warp(ctl.p_full);
+          ok = wait_all(ctl.dq_full, lt & 1);
+          if (ok) {
+            // dQ_part row t = query row qi*128 + t, scaled, added into the accumulator.
+            const int row = qi * kT + t;
+#pragma unroll 1
+            for (int h = 0; h < 2; ++h) {
+              uint32_t u[32];
+              tmem_ld32(t_lane + kColDQ + h * 32, u);
+              tmem_wait_ld();
+              if (row < N) {
+                float* dst = dq_acc + (static_cast<int64_t>(bh) * N + row) * kD + h * 32;
+#pragma unroll
+                for (int q4 = 0; q4 < 8; ++q4)
+                  red_add_v4(dst + 4 * q4, __uint_as_float(u[4 * q4]) * scale, __uint_as_float(u[4 * q4 + 1]) * scale,
+                             __uint_as_float(u[4 * q4 + 2]) * scale, __uint_as_float(u[4 * q4 + 3]) * scale);
+              }
+            }
+          }
+          ++lt;
+        }
+      }
+      arrive_warp(ctl.tile_free);
+    }
+    // dV and dK of this key tile (lane t = key k0 + t); zero when no query tile was live.
+    const int key = k0 + t;
+#pragma unroll 1
+    for (int h = 0; h < 2; ++h) {
+      uint32_t vw[16], kw[16];
+      if (ok && lt > 0) {
+        uint32_t u[32];
+        tmem_ld32(t_lane + kColDV + h * 32, u);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; ++e) vw[e] = pack2<BF16>(__uint_as_float(u[2 * e]), __uint_as_float(u[2 * e + 1]));
+        tmem_ld32(t_lane + kColDK + h * 32, u);
+        tmem_wait_ld();
+#pragma unroll
+        for (int e = 0; e < 16; ++e)
+          kw[e] = pack2<BF16>(__uint_as_float(u[2 * e]) * scale, __uint_as_float(u[2 * e + 1]) * scale);
+      } else {
+#pragma unroll
+        for (int e = 0; e < 16; ++e) vw[e] = kw[e] = 0u;
+      }
+      if (key < N && ctl.abort_flag == 0) {
+        uint4* dvr = reinterpret_cast<uint4*>(dv + (static_cast<int64_t>(bh) * N + key) * kD + h * 32);
+        uint4* dkr = reinterpret_cast<uint4*>(dk + (static_cast<int64_t>(bh) * N + key) * kD + h * 32);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          dvr[q] = make_uint4(vw[4 * q], vw[4 * q + 1], vw[4 * q + 2], vw[4 * q + 3]);
+          dkr[q] = make_uint4(kw[4 * q], kw[4 * q + 1], kw[4 * q + 2], kw[4 * q + 3]);
+        }
+      }
+    }
+    if (!ok && lane == 0) fail();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <bool BF16>
+int launch(const BwdParams& p, const char** msg) {
+  const int64_t BH = p.B * p.H;
+  const int64_t N = p.N;
+  const int64_t W = (N + 31) / 32;
+  const int64_t KT = (N + kT - 1) / kT;
+  const int64_t QT = (N + kT - 1) / kT;
+  if (BH * KT > 0x7FFFFFFFll) {
+    *msg = "backward: batch*heads too large";
+    return kErrArg;
+  }
+  CUtensorMap mq, mk, mv, mdo;
+  if (!make_tensor_map_3d(&mq, p.q, p.dtype, kD, BH, N, kT) || !make_tensor_map_3d(&mk, p.k, p.dtype, kD, BH, N, kT) ||
+      !make_tensor_map_3d(&mv, p.v, p.dtype, kD, BH, N, kT) ||
+      !make_tensor_map_3d(&mdo, p.dout, p.dtype, kD, BH, N, kT)) {
+    *msg = "backward: cuTensorMapEncodeTiled failed (pointer alignment or driver entry point)";
+    return kErrCuda;
+  }
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    *msg = "backward: no current CUDA device";
+    return kErrCuda;
+  }
+  static bool smem_set[kMaxDevices] = {};
+  auto kern = attn_bwd_kernel<BF16>;
+  if (!smem_set[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+    if (e != cudaSuccess) {
+      *msg = cudaGetErrorString(e);
+      return kErrLaunch;
+    }
+    smem_set[dev] = true;
+  }
+  const int64_t rows = BH * N;
+  cudaError_t e = cudaMemsetAsync(p.dq_accum, 0, static_cast<size_t>(rows) * kD * sizeof(float), p.stream);
+  if (e == cudaSuccess) {
+    bwd_delta_kernel<BF16><<<static_cast<unsigned>((rows * 8 + 255) / 256), 256, 0, p.stream>>>(
+        static_cast<const uint4*>(p.dout), static_cast<const uint4*>(p.out), p.delta, rows);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) {
+    const int vec = (W % 4 == 0 && (reinterpret_cast<uintptr_t>(p.mask) & 15u) == 0) ? 1 : 0;
+    kern<<<static_cast<unsigned>(BH * KT), kThreads, kSmemBytes, p.stream>>>(
+        mq, mk, mv, mdo, p.mask, p.lse, p.delta, p.dq_accum, static_cast<uint16_t*>(p.dk),
+        static_cast<uint16_t*>(p.dv), static_cast<int>(N), static_cast<int>(W), static_cast<int>(KT),
+        static_cast<int>(QT), vec, p.scale, p.err_word, p.timeout_ns);
+    e = cudaGetLastError();
+  }
+  if (e == cudaSuccess) {
+    const int64_t n8 = rows * kD / 8;
+    bwd_dq_convert_kernel<BF16><<<static_cast<unsigned>((n8 + 255) / 256), 256, 0, p.stream>>>(
+        reinterpret_cast<const float4*>(p.dq_accum), static_cast<uint4*>(p.dq), n8);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) {
+    *msg = cudaGetErrorString(e);
+    return kErrLaunch;
+  }
+  return kOk;
+}
+
+}  // namespace
+
+int launch_attn_bwd(const BwdParams& p, const char** msg) {
+  if (p.D != kD) {
+    *msg = "backward: head dim must be 64";
+    return kErrUnsupportedD;
+  }
+  if (p.N > kMaxSeqLen) {
+    *msg = "backward: sequence length above the supported maximum (65536)";
+    return kErrUnsupportedN;
+  }
+  return p.dtype == 1 ? launch<true>(p, msg) : launch<false>(p, msg);
+}
+
+}  // namespace sma

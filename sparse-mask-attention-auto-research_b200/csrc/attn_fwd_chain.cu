@@ -951,33 +951,6 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ---------------------------------------------------------------- host side
 
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (fn == nullptr) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
-// [BH, N, D] view of a contiguous [B, H, N, D] tensor: boxes of 64 head dims
-// (one 128-byte swizzle span) by `rows` rows.
-bool map3d(CUtensorMap* m, const void* ptr, int dtype, int64_t D, int64_t BH, int64_t N, int rows) {
-  auto fn = encode_fn();
-  if (fn == nullptr) return false;
-  cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(BH)};
-  cuuint64_t strides[2] = {static_cast<cuuint64_t>(D * 2), static_cast<cuuint64_t>(N * D * 2)};
-  cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(rows), 1u};
-  cuuint32_t estr[3] = {1u, 1u, 1u};
-  return fn(m, dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
-            const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 template <int D, bool BF16>
 int launch(const AttnParams& p, const char** msg) {
   using C = ChainCfg<D>;
@@ -993,8 +966,8 @@ int launch(const AttnParams& p, const char** msg) {
     return kErrArg;
   }
   CUtensorMap mq, mk, mv, mo;
-  if (!map3d(&mq, p.q, p.dtype, D, BH, N, kBM) || !map3d(&mk, p.k, p.dtype, D, BH, N, C::kBN) ||
-      !map3d(&mv, p.v, p.dtype, D, BH, N, C::kBN) || !map3d(&mo, p.out, p.dtype, D, BH, N, kBM)) {
+  if (!make_tensor_map_3d(&mq, p.q, p.dtype, D, BH, N, kBM) || !make_tensor_map_3d(&mk, p.k, p.dtype, D, BH, N, C::kBN) ||
+      !make_tensor_map_3d(&mv, p.v, p.dtype, D, BH, N, C::kBN) || !make_tensor_map_3d(&mo, p.out, p.dtype, D, BH, N, kBM)) {
     *msg = "attention: cuTensorMapEncodeTiled failed (pointer alignment or driver entry point)";
     return kErrCuda;
   }

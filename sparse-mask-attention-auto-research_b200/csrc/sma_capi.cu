@@ -143,6 +143,54 @@ int sma_attn_fwd_occupancy(int dtype, const void* q, const void* k, const void* 
                        scale, stream);
 }
 
+int sma_attn_bwd(int dtype, const void* q, const void* k, const void* v, const void* out, const void* dout,
+                 const float* lse, const void* mask_packed, void* dq, void* dk, void* dv, float* dq_accum, float* delta,
+                 int64_t B, int64_t H, int64_t N, int64_t D, float scale, void* stream) {
+  if (dtype != SMA_DTYPE_FP16 && dtype != SMA_DTYPE_BF16)
+    return fail(sma::kErrDtype, "backward: unsupported dtype, need fp16 or bf16");
+  if (B < 0 || H < 0 || N < 0 || D <= 0) return fail(sma::kErrArg, "backward: bad dimension");
+  if (D != 64) return fail(sma::kErrUnsupportedD, "backward: head dim must be 64");
+  if (N > SMA_MAX_SEQ_LEN) return fail(sma::kErrUnsupportedN, "backward: sequence length above the supported maximum (65536)");
+  if (!(scale > 0.f) || !(scale < INFINITY)) return fail(sma::kErrArg, "backward: scale must be finite and > 0");
+  if (B == 0 || H == 0 || N == 0) return sma::kOk;
+  if (!q || !k || !v || !out || !dout || !lse || !mask_packed || !dq || !dk || !dv || !dq_accum || !delta)
+    return fail(sma::kErrArg, "backward: null pointer");
+  if (!aligned16(q) || !aligned16(k) || !aligned16(v) || !aligned16(out) || !aligned16(dout) || !aligned16(dq) ||
+      !aligned16(dk) || !aligned16(dv) || !aligned16(dq_accum))
+    return fail(sma::kErrArg, "backward: q/k/v/out/dout/dq/dk/dv/dq_accum must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(lse) & 3u) || (reinterpret_cast<uintptr_t>(delta) & 3u) ||
+      (reinterpret_cast<uintptr_t>(mask_packed) & 3u))
+    return fail(sma::kErrArg, "backward: lse/delta/mask_packed must be 4-byte aligned");
+  uint32_t* err = nullptr;
+  int rc = error_word(&err);
+  if (rc != sma::kOk) return rc;
+  sma::BwdParams p{};
+  p.dtype = dtype;
+  p.q = q;
+  p.k = k;
+  p.v = v;
+  p.out = out;
+  p.dout = dout;
+  p.lse = lse;
+  p.mask = static_cast<const uint32_t*>(mask_packed);
+  p.dq = dq;
+  p.dk = dk;
+  p.dv = dv;
+  p.dq_accum = dq_accum;
+  p.delta = delta;
+  p.B = B;
+  p.H = H;
+  p.N = N;
+  p.D = D;
+  p.scale = scale;
+  p.err_word = err;
+  p.timeout_ns = g_timeout_ns;
+  p.stream = static_cast<cudaStream_t>(stream);
+  const char* msg = nullptr;
+  rc = sma::launch_attn_bwd(p, &msg);
+  return rc == sma::kOk ? rc : fail(rc, msg);
+}
+
 int sma_device_status(void* stream, int clear) {
   uint32_t* err = nullptr;
   int rc = error_word(&err);

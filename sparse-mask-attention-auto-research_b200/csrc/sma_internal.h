@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace sma {
@@ -51,6 +52,35 @@ int launch_pack_mask_occ(const uint8_t* mask, uint32_t* packed, uint32_t* occ, i
                          cudaStream_t stream, const char** msg);
 
 int launch_attn_fwd(const AttnParams& p, const char** msg);
+
+struct BwdParams {
+  int dtype;                  // 0 = fp16, 1 = bf16
+  const void* q;              // [B, H, N, D] contiguous, as for the forward
+  const void* k;
+  const void* v;
+  const void* out;            // the forward's O
+  const void* dout;           // upstream gradient of O
+  const float* lse;           // [B, H, N] the forward's LSE (natural log, -FLT_MAX for empty rows)
+  const uint32_t* mask;       // packed mask
+  void* dq;                   // [B, H, N, D] outputs
+  void* dk;
+  void* dv;
+  float* dq_accum;            // [B, H, N, D] FP32 scratch
+  float* delta;               // [B, H, N] FP32 scratch
+  int64_t B, H, N, D;
+  float scale;
+  uint32_t* err_word;
+  uint64_t timeout_ns;
+  cudaStream_t stream;
+};
+
+// Backward (attn_bwd.cu): head dim 64.
+int launch_attn_bwd(const BwdParams& p, const char** msg);
+
+// TMA map of the [BH, N, D] view of a contiguous [B, H, N, D] fp16/bf16
+// tensor: boxes of 64 head dims (one 128-byte swizzle span) by `rows` rows,
+// 128-byte swizzle (tma_map.cu).
+bool make_tensor_map_3d(CUtensorMap* m, const void* ptr, int dtype, int64_t D, int64_t BH, int64_t N, int rows);
 
 // Launches `kern` with programmatic stream serialisation: its CTAs may start
 // (and run their set-up) while the previous kernel in the stream finishes;

@@ -287,10 +287,11 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t saddr, uint32_t lbo
 // Instruction descriptor for kind::f16 with FP32 accumulation.
 //   bf16:   0 = fp16 operands, 1 = bf16 operands (A and B always the same type)
 //   b_mn:   0 = B is K-major, 1 = B is MN-major (A is always K-major here)
-__host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, int bf16, int b_mn) {
+__host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, int bf16, int b_mn, int a_mn = 0) {
   return (1u << 4)                                         // D format: f32
          | (static_cast<uint32_t>(bf16) << 7)              // A format
          | (static_cast<uint32_t>(bf16) << 10)             // B format
+         | (static_cast<uint32_t>(a_mn) << 15)             // A major (1: M contiguous)
          | (static_cast<uint32_t>(b_mn) << 16)             // B major
          | (static_cast<uint32_t>(N >> 3) << 17)           // N / 8
          | (static_cast<uint32_t>(M >> 4) << 24);          // M / 16

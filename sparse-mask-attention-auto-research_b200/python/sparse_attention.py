@@ -18,8 +18,9 @@ Differences from the reference, all deliberate:
     RuntimeError (the FP32 reference lives in the test oracle, not here).
   * ``sparse_attention_func`` works (the reference passes lse=None to a
     binding that rejects it).
-  * ``SparseAttentionFunction.backward`` raises: the reference's CUDA
-    backward is an unbound stub (AttributeError when called).
+  * ``SparseAttentionFunction.backward`` runs the backward kernel (head dim
+    64); the reference's CUDA backward is an unbound stub (AttributeError
+    when called) and its CPU formulas define the result.
   * ``sparse_attention`` / ``sparse_attention_func`` pack long or large
     masks with the fused packer, which also writes the per-query-tile map of
     live key tiles the attention kernel then uses (same results, no
@@ -50,10 +51,13 @@ class SparseAttentionFunction(Function):
 
     @staticmethod
     def backward(ctx, dout):
-        raise RuntimeError(
-            "sparse_attention backward is not implemented by the B200 kernels "
-            "(the reference's CUDA backward is an unbound stub as well)"
-        )
+        """dq, dk, dv through the backward kernel (reference :82-114; its
+        CUDA entry is unbound, its CPU formulas define the result)."""
+        q, k, v, out, lse, mask_packed, mask_bool = ctx.saved_tensors
+        dout = dout.contiguous()
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+        sparse_attn_cuda.backward(dout, q, k, v, out, lse, mask_packed, dq, dk, dv, ctx.scale)
+        return dq, dk, dv, None, None, None, None, None
 
 
 def _pack_for_attention(mask, head_dim):

@@ -106,6 +106,43 @@ def forward(q, k, v, mask_packed, out, lse, scale, is_training, occupancy=None):
         )
 
 
+def backward(dout, q, k, v, out, lse, mask_packed, dq, dk, dv, scale):
+    """Sparse attention backward with the signature the reference calls
+    (python/sparse_attention.py:93-96; never bound by its csrc/binding.cpp).
+    Writes dq, dk, dv (shape and dtype of q) from the forward's out and lse.
+    Head dim 64 only; the FP32 scratch it needs is allocated here."""
+    _require(q.is_cuda, "q must be CUDA tensor")
+    _require(q.dim() == 4, "q must be 4D")
+    _require(q.dtype in _DTYPES, "Unsupported dtype, need BF16 or FP16")
+    B, H, N, D = q.shape
+    for name, t in (("k", k), ("v", v), ("out", out), ("dout", dout), ("dq", dq), ("dk", dk), ("dv", dv)):
+        _require(t.device == q.device, f"{name} must be on the same device as q")
+        _require(t.shape == q.shape, f"{name} must have the shape of q {tuple(q.shape)}")
+        _require(t.dtype == q.dtype, f"{name} must have the dtype of q")
+        _require(t.is_contiguous(), f"{name} must be contiguous")
+    _require(q.is_contiguous(), "q must be contiguous")
+    _require(lse.device == q.device and lse.dtype == torch.float32, "lse must be float32 on the device of q")
+    _require(tuple(lse.shape) == (B, H, N) and lse.is_contiguous(), f"lse must be contiguous with shape {(B, H, N)}")
+    n_words = (N + 31) // 32
+    _require(mask_packed.device == q.device, "mask_packed must be on the same device as q")
+    _require(mask_packed.dtype in (torch.int32, torch.uint32), "mask_packed must be int32/uint32")
+    _require(
+        tuple(mask_packed.shape) == (B, H, N, n_words) and mask_packed.is_contiguous(),
+        f"mask_packed must be contiguous with shape {(B, H, N, n_words)}",
+    )
+    dq_accum = torch.empty((B, H, N, D), dtype=torch.float32, device=q.device)
+    delta = torch.empty((B, H, N), dtype=torch.float32, device=q.device)
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        _lib.check(
+            lib.sma_attn_bwd(
+                _DTYPES[q.dtype], q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(), dout.data_ptr(),
+                lse.data_ptr(), mask_packed.data_ptr(), dq.data_ptr(), dk.data_ptr(), dv.data_ptr(),
+                dq_accum.data_ptr(), delta.data_ptr(), B, H, N, D, float(scale), _stream_ptr(q.device),
+            )
+        )
+
+
 def pack_mask(mask):
     """bool [B, H, N, N] -> int32 [B, H, N, ceil(N/32)] (reference csrc/binding.cpp:49-66)."""
     _require(mask.is_cuda, "mask must be CUDA tensor")

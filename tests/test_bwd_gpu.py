@@ -1,0 +1,124 @@
+"""The backward kernel (sma_attn_bwd) against the reference's backward
+formulas: golden fixtures made by the reference's own CPU backward
+(python/sparse_attention.py:97-111), and the oracle restatement of it on
+workload-shaped inputs.  The forward's out and lse come from this library's
+forward kernel, as they do in training.
+
+Tolerance: max |grad - FP32 reference| <= tol * max |FP32 reference| per
+gradient, tol = 1.5e-2 (fp16) / 4e-2 (bf16).  P and dS are rounded to the
+input dtype for the tensor-core products (as in the forward) and the output
+gradients to the input dtype; the reference works in FP32 throughout."""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden_ids, golden_paths, load_golden
+from oracle import oracle
+from python import pack_mask, sparse_attention, sparse_attn_cuda, workloads
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda:0"
+TOL = {torch.float16: 1.5e-2, torch.bfloat16: 4e-2}
+
+
+def fwd_bwd(q, k, v, m, dout):
+    B, H, N, D = q.shape
+    scale = 1.0 / math.sqrt(D)
+    packed = pack_mask(m)
+    out = torch.empty_like(q)
+    lse = torch.empty(B, H, N, device=q.device, dtype=torch.float32)
+    sparse_attn_cuda.forward(q, k, v, packed, out, lse, scale, True)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    sparse_attn_cuda.backward(dout, q, k, v, out, lse, packed, dq, dk, dv, scale)
+    sparse_attn_cuda.device_status()
+    return dq, dk, dv
+
+
+def check_grads(got, want, dtype, mask):
+    for g, w, name in zip(got, want, ("dq", "dk", "dv")):
+        g = g.float().cpu()
+        w = torch.as_tensor(w).float()
+        scale = max(float(w.abs().max()), 1e-6)
+        err = float((g - w).abs().max())
+        assert err <= TOL[dtype] * scale, f"{name}: max abs err {err:.3e} vs max |ref| {scale:.3e}"
+        assert torch.isfinite(g).all(), f"{name} has non-finite values"
+    m = torch.as_tensor(mask)
+    empty_rows = ~m.any(dim=-1)
+    empty_cols = ~m.any(dim=-2)
+    assert torch.all(got[0].float().cpu()[empty_rows] == 0), "rows with no kept key get dq = 0"
+    assert torch.all(got[1].float().cpu()[empty_cols] == 0), "keys no row attends get dk = 0"
+    assert torch.all(got[2].float().cpu()[empty_cols] == 0), "keys no row attends get dv = 0"
+
+
+D64 = [p for p in golden_paths("bwd") if "D128" not in p]
+
+
+@pytest.mark.parametrize("path", D64, ids=[i for i in golden_ids("bwd") if "D128" not in i])
+def test_golden(path):
+    case = load_golden(path)
+    q, k, v, dout, m = (case[x].to(DEV) for x in ("q", "k", "v", "dout", "mask"))
+    got = fwd_bwd(q, k, v, m, dout)
+    check_grads(got, (case["dq"], case["dk"], case["dv"]), case["dtype"], case["mask"])
+
+
+@pytest.mark.parametrize("name,kw", [("c1", dict(B=2)), ("c4", dict(B=1, H=2)), ("c2", dict(B=4, dtype=torch.bfloat16))])
+def test_workload_vs_oracle(name, kw):
+    q, k, v, m = workloads.make_inputs(name, seed=11, device=DEV, **kw)
+    g = torch.Generator(device=DEV).manual_seed(12)
+    dout = torch.randn(q.shape, generator=g, device=DEV).to(q.dtype)
+    got = fwd_bwd(q, k, v, m, dout)
+    D = q.shape[-1]
+    want = oracle.attention_backward(*(x.float().cpu().numpy() for x in (q, k, v)), m.cpu().numpy(),
+                                     1 / math.sqrt(D), dout.float().cpu().numpy())
+    check_grads(got, want, q.dtype, m.cpu())
+
+
+def test_autograd_through_public_api():
+    """loss.backward() through sparse_attention() gives the oracle's gradients."""
+    q, k, v, m = workloads.make_inputs("c1", seed=13, device=DEV, B=1, H=2)
+    q, k, v = (x.clone().requires_grad_(True) for x in (q, k, v))
+    g = torch.Generator(device=DEV).manual_seed(14)
+    w = torch.randn(q.shape, generator=g, device=DEV).to(q.dtype)
+    out = sparse_attention(q, k, v, m)
+    (out.float() * w.float()).sum().backward()
+    want = oracle.attention_backward(*(x.detach().float().cpu().numpy() for x in (q, k, v)), m.cpu().numpy(),
+                                     1 / math.sqrt(q.shape[-1]), w.float().cpu().numpy())
+    check_grads((q.grad, k.grad, v.grad), want, q.dtype, m.cpu())
+
+
+def test_fp32_inputs_backward():
+    """fp32 q/k/v run in bf16 like the forward; gradients come back in fp32."""
+    q, k, v, m = workloads.make_inputs("c2", seed=15, device=DEV, B=1, H=2)
+    q, k, v = (x.float().requires_grad_(True) for x in (q, k, v))
+    out = sparse_attention(q, k, v, m)
+    out.sum().backward()
+    assert q.grad.dtype == torch.float32 and torch.isfinite(q.grad).all()
+    want = oracle.attention_backward(*(x.detach().bfloat16().float().cpu().numpy() for x in (q, k, v)),
+                                     m.cpu().numpy(), 1 / 8.0, np.ones(q.shape, np.float32))
+    check_grads((q.grad, k.grad, v.grad), want, torch.bfloat16, m.cpu())
+
+
+def test_all_masked_gives_zero_gradients():
+    N = 256
+    g = torch.Generator(device=DEV).manual_seed(16)
+    q, k, v, dout = (torch.randn(1, 2, N, 64, generator=g, device=DEV).half() for _ in range(4))
+    m = torch.zeros(1, 2, N, N, dtype=torch.bool, device=DEV)
+    dq, dk, dv = fwd_bwd(q, k, v, m, dout)
+    assert not dq.any() and not dk.any() and not dv.any()
+
+
+def test_long_sequence_backward():
+    """N = 3000 (ragged tiles, 24 key tiles), checked on sampled rows of dq
+    and sampled keys of dk/dv against the oracle."""
+    N, H = 3000, 1
+    g = torch.Generator(device=DEV).manual_seed(17)
+    q, k, v, dout = (torch.randn(1, H, N, 64, generator=g, device=DEV).half() for _ in range(4))
+    m = torch.rand(1, H, N, N, generator=g, device=DEV) < 0.05
+    m[..., 100:300, :] = False
+    dq, dk, dv = fwd_bwd(q, k, v, m, dout)
+    want = oracle.attention_backward(*(x.float().cpu().numpy() for x in (q, k, v)), m.cpu().numpy(),
+                                     1 / 8.0, dout.float().cpu().numpy())
+    check_grads((dq, dk, dv), want, torch.float16, m.cpu())
