@@ -57,6 +57,8 @@ def parse_args():
     ap.add_argument("--cpu-seconds", type=float, default=10.0, help="budget of the CPU baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=50)
+    ap.add_argument("--pass", dest="which", default="forward", choices=["forward", "backward"],
+                    help="backward: time sparse_attn_cuda.backward (one GPU) instead of the forward step")
     return ap.parse_args()
 
 
@@ -442,10 +444,91 @@ def run_ours(args):
     return 0
 
 
+def run_backward(args):
+    """One GPU: the backward (dq, dk, dv from dout and the forward's out and
+    lse) on the workload, inputs resident in HBM, L2 flushed before every
+    step.  Prints one JSON line in the forward's format."""
+    rank, world, local = dist_env()
+    if world != 1 or args.gpus != 1:
+        raise SystemExit("--pass backward runs on one GPU")
+    from python import pack_mask, sparse_attn_cuda, workloads
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    cfg = workloads.CONFIGS[args.config]
+    B, H, N, D = cfg["B"], cfg["H"], cfg["N"], cfg["D"]
+    if D != 64:
+        print(json.dumps({"metric": "backward", "unavailable": "the backward kernel takes head dim 64 only"}))
+        return 0
+    q, k, v, m = workloads.make_inputs(args.config, seed=args.seed, device=dev)
+    g = torch.Generator(device=dev).manual_seed(args.seed + 7)
+    dout = torch.randn(q.shape, generator=g, device=dev).to(q.dtype)
+    scale = 1.0 / math.sqrt(D)
+    packed = pack_mask(m)
+    out = torch.empty_like(q)
+    lse = torch.empty(B, H, N, device=dev, dtype=torch.float32)
+    sparse_attn_cuda.forward(q, k, v, packed, out, lse, scale, True)
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    flush = torch.empty(FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        sparse_attn_cuda.backward(dout, q, k, v, out, lse, packed, dq, dk, dv, scale)
+
+    for _ in range(args.warmup):
+        flush.zero_()
+        step()
+    sparse_attn_cuda.device_status()
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+    sampler = ClockSampler(dev)
+    torch.cuda.synchronize(dev)
+    for i in range(args.steps):
+        flush.zero_()
+        evs[i][0].record(stream)
+        step()
+        evs[i][1].record(stream)
+    torch.cuda.synchronize(dev)
+    clocks = sampler.stop()
+    sparse_attn_cuda.device_status()
+    ms = sorted(e[0].elapsed_time(e[1]) for e in evs)
+    p50 = ms[len(ms) // 2]
+    peaks = load_peaks()
+    flops = workloads.backward_flops(B, H, N, D)
+    nbytes = workloads.backward_bytes(B, H, N, D)
+    live = workloads.live_tile_fraction(m, 128, 128)
+    mma_flops = flops * live  # the kernel's five products run on live 128x128 tile pairs only
+    line = {
+        "metric": "backward dense-equiv TFLOPS (10*B*H*N^2*D / p50 step)",
+        "value": flops / (p50 * 1e-3) / 1e12,
+        "unit": "TFLOPS",
+        "n_gpus": 1,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": p50,
+        "higher_is_better": True,
+        "dtype": {torch.float16: "fp16", torch.bfloat16: "bf16"}[cfg["dtype"]],
+        "data": "synthetic (seeded N(0,1) q/k/v/dout, seeded masks per the workload recipe)",
+        "config": {"workload": f"{args.config}: {workloads.describe(args.config)}", "pass": "backward",
+                   "l2": "flushed (512 MiB memset) before every timed step"},
+        "roofline": {"bound": "hbm", "achieved": nbytes / (p50 * 1e-3) / 1e9, "peak": peaks["hbm_gbs"],
+                     "unit": "GB/s", "frac": nbytes / (p50 * 1e-3) / 1e9 / peaks["hbm_gbs"],
+                     "algorithmic_bytes_per_step": nbytes, "peak_source": peaks["source"]},
+        "roofline_tensor": {"achieved": mma_flops / (p50 * 1e-3) / 1e12, "peak": peaks["bf16_tflops"],
+                            "unit": "TFLOP/s", "frac": mma_flops / (p50 * 1e-3) / 1e12 / peaks["bf16_tflops"],
+                            "live_tile_fraction": live},
+        "clocks": clocks,
+        "gpu_launches": 3 * args.steps,
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse_args()
     if args.impl == "reference":
         return run_reference(args)
+    if args.which == "backward":
+        return run_backward(args)
     return run_ours(args)
 
 

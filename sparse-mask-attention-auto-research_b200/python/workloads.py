@@ -118,6 +118,20 @@ def attn_bytes(B, H, N, D, elem=2, with_lse=True):
     return qkvo + packed + lse
 
 
+def backward_flops(B, H, N, D):
+    """Dense-equivalent FLOPs of one backward: five N x N x D products
+    (S, dP, dV, dK, dQ), 10*B*H*N^2*D."""
+    return 10.0 * B * H * N * N * D
+
+
+def backward_bytes(B, H, N, D, elem=2):
+    """Algorithmic HBM bytes of the backward: read Q, K, V, O, dO, the packed
+    mask and the LSE once, write dQ, dK, dV.  (The FP32 dQ accumulator adds
+    a clear, the partial sums and a final read on top.)"""
+    bh = B * H
+    return 8 * bh * N * D * elem + bh * N * ((N + 31) // 32) * 4 + bh * N * 4
+
+
 def pack_bytes(B, H, N):
     """Algorithmic HBM bytes of pack_mask: read N^2 bytes, write N^2/8."""
     bh = B * H
