@@ -128,6 +128,18 @@ SMA_API int sma_attn_bwd(int dtype, const void* q, const void* k, const void* v,
                          float* delta, int64_t B, int64_t H, int64_t N, int64_t D, float scale, void* stream);
 
 /*
+ * sma_attn_bwd with the FP32 scratch taken from a fixed 32 MiB device array
+ * inside the library (one per device, found once per device with
+ * cudaGetSymbolAddress): no memory is allocated and no allocating routine is
+ * called.  Inputs whose B*H*N*(D+1) floats exceed the array return
+ * SMA_ERR_ARG.  Calls sharing a device share the array: order them on one
+ * stream.  No reference counterpart.
+ */
+SMA_API int sma_attn_bwd_noalloc(int dtype, const void* q, const void* k, const void* v, const void* out,
+                                 const void* dout, const float* lse, const void* mask_packed, void* dq, void* dk,
+                                 void* dv, int64_t B, int64_t H, int64_t N, int64_t D, float scale, void* stream);
+
+/*
  * Synchronise `stream`, then report whether any kernel of this library on the
  * current device gave up a bounded device-side wait since the last clear
  * (SMA_ERR_TIMEOUT), or whether the stream holds a CUDA error (SMA_ERR_CUDA).

@@ -50,6 +50,29 @@ int error_word(uint32_t** out) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Fixed device scratch of sma_attn_bwd_noalloc: the FP32 dQ accumulator
+// (B*H*N*D floats) followed by Delta (B*H*N floats).  One copy per device,
+// part of the module image, so that entry point allocates nothing.
+constexpr int64_t kNoAllocScratchFloats = int64_t{8} << 20;  // 32 MiB
+static __device__ __align__(256) float g_bwd_noalloc_scratch[kNoAllocScratchFloats];
+float* g_noalloc_ptr[kMaxDevices] = {};
+
+// Device address of the fixed scratch on the current device (looked up once per device).
+int noalloc_scratch(float** out) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
+  if (dev < 0 || dev >= kMaxDevices) return fail(sma::kErrCuda, "device index out of range");
+  if (g_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_bwd_noalloc_scratch);
+    if (e != cudaSuccess) return fail_cuda(e, "cudaGetSymbolAddress");
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return sma::kOk;
+}
+
 }  // namespace
 
 extern "C" {
@@ -189,6 +212,23 @@ int sma_attn_bwd(int dtype, const void* q, const void* k, const void* v, const v
   const char* msg = nullptr;
   rc = sma::launch_attn_bwd(p, &msg);
   return rc == sma::kOk ? rc : fail(rc, msg);
+}
+
+int sma_attn_bwd_noalloc(int dtype, const void* q, const void* k, const void* v, const void* out, const void* dout,
+                         const float* lse, const void* mask_packed, void* dq, void* dk, void* dv, int64_t B,
+                         int64_t H, int64_t N, int64_t D, float scale, void* stream) {
+  if (B < 0 || H < 0 || N < 0 || D <= 0) return fail(sma::kErrArg, "backward: bad dimension");
+  if (B == 0 || H == 0 || N == 0) return sma::kOk;
+  // dQ accumulator + Delta must fit the fixed scratch (checked without overflow).
+  const int64_t per_bh = N * (D + 1);
+  if (D > 4096 || N > SMA_MAX_SEQ_LEN || B > kNoAllocScratchFloats || H > kNoAllocScratchFloats ||
+      B * H > kNoAllocScratchFloats / per_bh)
+    return fail(sma::kErrArg, "backward (no-alloc): B*H*N*(D+1) floats exceed the fixed 32 MiB scratch");
+  float* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc != sma::kOk) return rc;
+  return sma_attn_bwd(dtype, q, k, v, out, dout, lse, mask_packed, dq, dk, dv, scratch, scratch + B * H * N * D, B,
+                      H, N, D, scale, stream);
 }
 
 int sma_device_status(void* stream, int clear) {

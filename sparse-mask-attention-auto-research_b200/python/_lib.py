@@ -46,6 +46,10 @@ SIGNATURES = {
         [ctypes.c_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
          ctypes.c_float, _vp],
     ),
+    "sma_attn_bwd_noalloc": (
+        ctypes.c_int,
+        [ctypes.c_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, ctypes.c_float, _vp],
+    ),
     "sma_device_status": (ctypes.c_int, [_vp, ctypes.c_int]),
     "sma_set_wait_timeout_ns": (ctypes.c_int, [ctypes.c_uint64]),
     "sma_debug_wait_probe": (ctypes.c_int, [ctypes.c_uint64, _vp]),
