@@ -50,31 +50,33 @@ constexpr int kTmemCols = 512;
 constexpr float kLog2e = 1.44269504088896340736f;
 constexpr int kMaxDevices = 64;
 
+// Query tiles are staged in two buffers (b = tile index & 1), so the loader
+// fills tile i+1 while tile i is computed.
 struct BwdCtl {
-  uint64_t kv_full;    // K and V landed
-  uint64_t ld_full;    // query tile staged (Q, dO by TMA; mask, LSE, Delta by the loader warp)
-  uint64_t st_full;    // S^T and dP^T complete
-  uint64_t p_full;     // P^T, dS^T in TMEM and dS in shared memory (4 compute warps)
-  uint64_t dq_full;    // dV, dK, dQ_part MMAs complete
-  uint64_t tile_free;  // compute warps and MMA issuer done with the query tile (5 arrivals)
+  uint64_t kv_full;       // K and V landed
+  uint64_t ld_full[2];    // query tile staged in buffer b (Q, dO by TMA; mask, LSE, Delta by the loader warp)
+  uint64_t st_full;       // S^T and dP^T complete
+  uint64_t p_full;        // P^T, dS^T in TMEM and dS in shared memory (4 compute warps)
+  uint64_t dq_full;       // dV, dK, dQ_part MMAs complete
+  uint64_t tile_free[2];  // compute warps and MMA issuer done with buffer b (5 arrivals)
   uint64_t drain;
   uint32_t tmem_base;
-  uint32_t live;
+  uint32_t live[2];
   uint32_t abort_flag;
 };
 
-// Shared memory: K | V | Q | dO (16 KiB each, 128-byte swizzle) | dS (two
-// 16 KiB M-major chunks of 64 queries) | mask words [4][128] | lse2 [128] |
-// Delta [128] | control.
-constexpr int kOffK = 0, kOffV = kTileBytes, kOffQ = 2 * kTileBytes, kOffDO = 3 * kTileBytes;
-constexpr int kOffDS = 4 * kTileBytes;
+// Shared memory: K | V | Q[2] | dO[2] (16 KiB each, 128-byte swizzle) | dS
+// (two 16 KiB M-major chunks of 64 queries) | mask words [2][4][128] |
+// lse2 [2][128] | Delta [2][128] | control.
+constexpr int kOffK = 0, kOffV = kTileBytes, kOffQ = 2 * kTileBytes, kOffDO = 4 * kTileBytes;
+constexpr int kOffDS = 6 * kTileBytes;
 constexpr int kOffMask = kOffDS + 2 * kTileBytes;
-constexpr int kOffLse = kOffMask + 4 * kT * 4;
-constexpr int kOffDelta = kOffLse + kT * 4;
-constexpr int kOffCtl = kOffDelta + kT * 4;
+constexpr int kOffLse = kOffMask + 2 * 4 * kT * 4;
+constexpr int kOffDelta = kOffLse + 2 * kT * 4;
+constexpr int kOffCtl = kOffDelta + 2 * kT * 4;
 // Above half of the SM's shared memory, so one CTA holds an SM (its TMEM
 // allocation takes all 512 columns).
-constexpr size_t kSmemBytes = 120 * 1024;
+constexpr size_t kSmemBytes = 136 * 1024;
 static_assert(kOffCtl + sizeof(BwdCtl) <= kSmemBytes, "shared memory layout");
 
 __device__ __forceinline__ float ex2f(float x) {
@@ -163,8 +165,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     return;
   }
   BwdCtl& ctl = *reinterpret_cast<BwdCtl*>(smem + kOffCtl);
-  uint32_t* s_mask = reinterpret_cast<uint32_t*>(smem + kOffMask);  // word w of query row i at [w * kT + i]
-  float* s_lse = reinterpret_cast<float*>(smem + kOffLse);          // LSE * log2(e) per query row
+  // Per buffer b: word w of query row i at s_mask[b * 4 * kT + w * kT + i];
+  // LSE * log2(e) and Delta per query row at s_lse / s_delta [b * kT + i].
+  uint32_t* s_mask = reinterpret_cast<uint32_t*>(smem + kOffMask);
+  float* s_lse = reinterpret_cast<float*>(smem + kOffLse);
   float* s_delta = reinterpret_cast<float*>(smem + kOffDelta);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -175,14 +179,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (threadIdx.x == 128) {
     mbar_init(smem_u32(&ctl.kv_full), 1);
-    mbar_init(smem_u32(&ctl.ld_full), 1);
     mbar_init(smem_u32(&ctl.st_full), 1);
     mbar_init(smem_u32(&ctl.p_full), 4);
     mbar_init(smem_u32(&ctl.dq_full), 1);
-    mbar_init(smem_u32(&ctl.tile_free), 5);  // 4 compute warps + the MMA issuer
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&ctl.ld_full[b]), 1);
+      mbar_init(smem_u32(&ctl.tile_free[b]), 5);  // 4 compute warps + the MMA issuer
+      ctl.live[b] = 0;
+    }
     mbar_init(smem_u32(&ctl.drain), 1);
     ctl.abort_flag = 0;
-    ctl.live = 0;
     fence_barrier_init();
     fence_proxy_async_smem();
   }
@@ -215,10 +221,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     int last_copy = -1;  // last query tile whose Q/dO copies were started
     for (int qi = 0; qi < QT; ++qi) {
-      // The previous query tile's staging is free once the compute warps and
-      // the MMA issuer are done with it (its MMAs have completed by then).
-      if (qi > 0 &&
-          !__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&ctl.tile_free), (qi - 1) & 1, abort_flag, timeout_ns))) {
+      const int b = qi & 1;
+      // Buffer b is free once the compute warps and the MMA issuer are done
+      // with tile qi-2 (its MMAs have completed by then).
+      if (qi >= 2 && !__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&ctl.tile_free[b]), ((qi - 2) >> 1) & 1,
+                                                                 abort_flag, timeout_ns))) {
         ok = false;
         break;
       }
@@ -251,23 +258,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
 #pragma unroll
         for (int w = 0; w < 4; ++w) {
-          s_mask[w * kT + i] = w4[w];
+          s_mask[b * 4 * kT + w * kT + i] = w4[w];
           any |= w4[w];
         }
-        s_lse[i] = l2;
-        s_delta[i] = de;
+        s_lse[b * kT + i] = l2;
+        s_delta[b * kT + i] = de;
       }
       const bool live = __any_sync(0xffffffffu, any != 0u);
       __syncwarp();
       if (lane == 0) {
-        ctl.live = live ? 1u : 0u;
+        ctl.live[b] = live ? 1u : 0u;
         if (live) {
-          mbar_arrive_expect_tx(smem_u32(&ctl.ld_full), 2 * kTileBytes);
-          tma_load_3d(base + kOffQ, &tm_q, smem_u32(&ctl.ld_full), 0, i0, bh);
-          tma_load_3d(base + kOffDO, &tm_do, smem_u32(&ctl.ld_full), 0, i0, bh);
+          mbar_arrive_expect_tx(smem_u32(&ctl.ld_full[b]), 2 * kTileBytes);
+          tma_load_3d(base + kOffQ + b * kTileBytes, &tm_q, smem_u32(&ctl.ld_full[b]), 0, i0, bh);
+          tma_load_3d(base + kOffDO + b * kTileBytes, &tm_do, smem_u32(&ctl.ld_full[b]), 0, i0, bh);
           last_copy = qi;
         } else {
-          mbar_arrive(smem_u32(&ctl.ld_full));
+          mbar_arrive(smem_u32(&ctl.ld_full[b]));
         }
       }
     }
@@ -276,7 +283,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Let the copies this warp started land before the CTA exits.
       uint32_t zero = 0;
       mbar_wait_bounded(smem_u32(&ctl.kv_full), 0, &zero, timeout_ns);
-      if (last_copy >= 0) mbar_wait_bounded(smem_u32(&ctl.ld_full), last_copy & 1, &zero, timeout_ns);
+      for (int qi = last_copy - 1; qi <= last_copy; ++qi)
+        if (qi >= 0) mbar_wait_bounded(smem_u32(&ctl.ld_full[qi & 1]), (qi >> 1) & 1, &zero, timeout_ns);
     }
   } else if (warp == 5) {
     // ================================================================ MMA issuer
@@ -284,17 +292,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc_s = make_idesc_f16(kT, kT, BF16 ? 1 : 0, 0);       // S^T, dP^T (M = keys)
       constexpr uint32_t idesc_kv = make_idesc_f16(kT, kD, BF16 ? 1 : 0, 1);      // dV, dK (B M/N-major)
       constexpr uint32_t idesc_q = make_idesc_f16(kT, kD, BF16 ? 1 : 0, 1, 1);    // dQ (A and B M/N-major)
-      const uint32_t sK = base + kOffK, sV = base + kOffV, sQ = base + kOffQ, sDO = base + kOffDO;
-      const uint32_t sDS = base + kOffDS;
+      const uint32_t sK = base + kOffK, sV = base + kOffV, sDS = base + kOffDS;
       bool ok = mbar_wait_bounded(smem_u32(&ctl.kv_full), 0, abort_flag, timeout_ns);
       uint32_t lt = 0;  // live query tiles done
       for (int qi = 0; ok && qi < QT; ++qi) {
-        if (!mbar_wait_bounded(smem_u32(&ctl.ld_full), qi & 1, abort_flag, timeout_ns) ||
-            (qi > 0 && !mbar_wait_bounded(smem_u32(&ctl.tile_free), (qi - 1) & 1, abort_flag, timeout_ns))) {
+        const int b = qi & 1;
+        const uint32_t sQ = base + kOffQ + b * kTileBytes, sDO = base + kOffDO + b * kTileBytes;
+        // Tile qi's staging, and tile qi-1 finished (its TMEM results read).
+        if (!mbar_wait_bounded(smem_u32(&ctl.ld_full[b]), (qi >> 1) & 1, abort_flag, timeout_ns) ||
+            (qi > 0 && !mbar_wait_bounded(smem_u32(&ctl.tile_free[b ^ 1]), ((qi - 1) >> 1) & 1, abort_flag,
+                                          timeout_ns))) {
           ok = false;
           break;
         }
-        if (ctl.live != 0u) {
+        if (ctl.live[b] != 0u) {
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < kD / 16; ++kk)
@@ -329,7 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           mma_commit(smem_u32(&ctl.dq_full));
           ++lt;
         }
-        mbar_arrive(smem_u32(&ctl.tile_free));
+        mbar_arrive(smem_u32(&ctl.tile_free[b]));
       }
       if (!ok) fail();
       // Every MMA this thread issued must complete before TMEM is released.
@@ -342,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int t = threadIdx.x;  // key row of the tile for P^T / dS^T / dK / dV, query row for dQ_part
     const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
     const float c2 = scale * kLog2e;
-    const uint32_t* my_words = s_mask + (t >> 5) * kT;  // the word holding this key, for each query row
+    const int my_word = (t >> 5) * kT;  // the word holding this key, for each query row
     const int kb = t & 31;
     bool ok = true;
     uint32_t lt = 0;
@@ -358,8 +369,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(smem_u32(&bar));
     };
     for (int qi = 0; qi < QT; ++qi) {
-      if (ok) ok = wait_all(ctl.ld_full, qi & 1);
-      if (ok && ctl.live != 0u) {
+      const int b = qi & 1;
+      const uint32_t* my_words = s_mask + b * 4 * kT + my_word;
+      const float* t_lse = s_lse + b * kT;
+      const float* t_delta = s_delta + b * kT;
+      if (ok) ok = wait_all(ctl.ld_full[b], (qi >> 1) & 1);
+      if (ok && ctl.live[b] != 0u) {
         ok = wait_all(ctl.st_full, lt & 1);
         if (ok) {
 #pragma unroll 1
@@ -372,8 +387,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
             for (int e = 0; e < 32; e += 4) {
               const uint4 m4 = *reinterpret_cast<const uint4*>(my_words + c * 32 + e);
-              const float4 l4 = *reinterpret_cast<const float4*>(s_lse + c * 32 + e);
-              const float4 d4 = *reinterpret_cast<const float4*>(s_delta + c * 32 + e);
+              const float4 l4 = *reinterpret_cast<const float4*>(t_lse + c * 32 + e);
+              const float4 d4 = *reinterpret_cast<const float4*>(t_delta + c * 32 + e);
               const uint32_t mm[4] = {m4.x, m4.y, m4.z, m4.w};
               const float ll[4] = {l4.x, l4.y, l4.z, l4.w}, dd[4] = {d4.x, d4.y, d4.z, d4.w};
               float p[4], ds[4];
@@ -424,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ++lt;
         }
       }
-      arrive_warp(ctl.tile_free);
+      arrive_warp(ctl.tile_free[b]);
     }
     // dV and dK of this key tile (lane t = key k0 + t); zero when no query tile was live.
     const int key = k0 + t;
