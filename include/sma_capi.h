@@ -108,7 +108,7 @@ SMA_API int sma_attn_fwd_occupancy(int dtype, const void* q, const void* k, cons
                                    int64_t D, float scale, void* stream);
 
 /*
- * Masked-softmax attention backward for head dim 64: given the forward's
+ * Masked-softmax attention backward (head dims 64 and 128): given the forward's
  * inputs, its out and lse (as written by sma_attn_fwd with a non-NULL lse)
  * and the upstream gradient dout, writes dq, dk, dv ([B, H, N, D] of `dtype`):
  *   P = exp(scale * q k^T - lse) where the mask bit is set, else 0
@@ -116,7 +116,7 @@ SMA_API int sma_attn_fwd_occupancy(int dtype, const void* q, const void* k, cons
  *   dq = scale * dS k;  dk = scale * dS^T q
  * dq_accum (FP32 [B, H, N, D]) and delta (FP32 [B, H, N]) are caller-provided
  * scratch.  Rows with no set bit get dq = 0; keys no row attends get dk = dv = 0.
- * Needs D = 64, 16-byte aligned q/k/v/out/dout/dq/dk/dv/dq_accum.
+ * Needs D in {64, 128}, 16-byte aligned q/k/v/out/dout/dq/dk/dv/dq_accum.
  *
  * Replaces: sparse_attn_cuda.backward(dout, q, k, v, out, lse, mask_packed,
  *           dq, dk, dv, scale), called by python/sparse_attention.py:93-96 but

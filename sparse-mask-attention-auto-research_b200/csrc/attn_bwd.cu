@@ -1,4 +1,4 @@
-// Fused masked-softmax attention backward, head dim 64 (sm_100a).
+// Fused masked-softmax attention backward, head dims 64 and 128 (sm_100a).
 //
 // The reference binds no CUDA backward (python/sparse_attention.py:93-96 calls
 // sparse_attn_cuda.backward, which csrc/binding.cpp never defines); its CPU
@@ -27,9 +27,8 @@
 //
 // Warps (192 threads): 0-3 compute (thread t <-> TMEM lane t), 4 loader
 // (TMA of K, V, Q, dO; mask words, LSE and Delta of the query tile staged in
-// shared memory), 5 MMA issuer and TMEM owner.
-// TMEM (512 columns): S^T [0,128) (P^T over its first 64), dP^T [128,256)
-// (dS^T over its first 64), dV [256,320), dK [320,384), dQ_part [384,448).
+// shared memory), 5 MMA issuer and TMEM owner.  TMEM layout per head dim:
+// see BwdCfg.
 // Every wait is bounded and reports through the device error word.
 #include <cfloat>
 #include <cuda_bf16.h>
@@ -41,17 +40,42 @@
 namespace sma {
 namespace {
 
-constexpr int kD = 64;
 constexpr int kT = 128;  // query rows and keys per tile
 constexpr int kThreads = 192;
-constexpr int kTileBytes = kT * kD * 2;  // 16 KiB
-constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256, kColDK = 320, kColDQ = 384;
 constexpr int kTmemCols = 512;
+constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256;
 constexpr float kLog2e = 1.44269504088896340736f;
 constexpr int kMaxDevices = 64;
 
-// Query tiles are staged in two buffers (b = tile index & 1), so the loader
-// fills tile i+1 while tile i is computed.
+// Per head dim.  Tiles of K, V, Q, dO are kT rows of D/64 128-byte swizzle
+// chunks.  D = 64 stages query tiles in two buffers (the loader fills tile
+// i+1 while tile i is computed); D = 128 has shared memory for one.
+// TMEM: S^T [0,128) and dP^T [128,256) (P^T / dS^T packed over their first
+// 64 columns), dV [256, 256+D), dK [256+D, 256+2D); dQ_part in 64-column
+// halves: D = 64 at [384,448), D = 128 over the S^T / dP^T columns that
+// P^T / dS^T leave free, [64,128) and [192,256).
+template <int D>
+struct BwdCfg {
+  static_assert(D == 64 || D == 128, "head dim");
+  static constexpr int kDChunks = D / 64;
+  static constexpr int kTileBytes = kT * D * 2;  // 16 / 32 KiB
+  static constexpr int kQBufs = D == 64 ? 2 : 1;
+  static constexpr uint32_t kColDK = kColDV + D;
+  __host__ __device__ static constexpr uint32_t col_dq(int h) { return D == 64 ? 384u : (h == 0 ? 64u : 192u); }
+  static constexpr int kOffK = 0;
+  static constexpr int kOffV = kTileBytes;
+  static constexpr int kOffQ = 2 * kTileBytes;
+  static constexpr int kOffDO = kOffQ + kQBufs * kTileBytes;
+  static constexpr int kOffDS = kOffDO + kQBufs * kTileBytes;  // two 16 KiB M-major chunks of 64 queries
+  static constexpr int kOffMask = kOffDS + 2 * kT * 128;
+  static constexpr int kOffLse = kOffMask + kQBufs * 4 * kT * 4;
+  static constexpr int kOffDelta = kOffLse + kQBufs * kT * 4;
+  static constexpr int kOffCtl = kOffDelta + kQBufs * kT * 4;
+  // Above half of the SM's shared memory, so one CTA holds an SM (its TMEM
+  // allocation takes all 512 columns).
+  static constexpr size_t kSmemBytes = D == 64 ? 136 * 1024 : 168 * 1024;
+};
+
 struct BwdCtl {
   uint64_t kv_full;       // K and V landed
   uint64_t ld_full[2];    // query tile staged in buffer b (Q, dO by TMA; mask, LSE, Delta by the loader warp)
@@ -65,19 +89,10 @@ struct BwdCtl {
   uint32_t abort_flag;
 };
 
-// Shared memory: K | V | Q[2] | dO[2] (16 KiB each, 128-byte swizzle) | dS
-// (two 16 KiB M-major chunks of 64 queries) | mask words [2][4][128] |
-// lse2 [2][128] | Delta [2][128] | control.
-constexpr int kOffK = 0, kOffV = kTileBytes, kOffQ = 2 * kTileBytes, kOffDO = 4 * kTileBytes;
-constexpr int kOffDS = 6 * kTileBytes;
-constexpr int kOffMask = kOffDS + 2 * kTileBytes;
-constexpr int kOffLse = kOffMask + 2 * 4 * kT * 4;
-constexpr int kOffDelta = kOffLse + 2 * kT * 4;
-constexpr int kOffCtl = kOffDelta + 2 * kT * 4;
-// Above half of the SM's shared memory, so one CTA holds an SM (its TMEM
-// allocation takes all 512 columns).
-constexpr size_t kSmemBytes = 136 * 1024;
-static_assert(kOffCtl + sizeof(BwdCtl) <= kSmemBytes, "shared memory layout");
+// Shared memory: K | V | Q[kQBufs] | dO[kQBufs] | dS | mask words
+// [kQBufs][4][128] | lse2 [kQBufs][128] | Delta [kQBufs][128] | control.
+static_assert(BwdCfg<64>::kOffCtl + sizeof(BwdCtl) <= BwdCfg<64>::kSmemBytes, "shared memory layout");
+static_assert(BwdCfg<128>::kOffCtl + sizeof(BwdCtl) <= BwdCfg<128>::kSmemBytes, "shared memory layout");
 
 __device__ __forceinline__ float ex2f(float x) {
   float y;
@@ -116,13 +131,14 @@ __device__ __forceinline__ uint32_t valid_bits(int cw, int N) {
   return valid >= 32 ? 0xFFFFFFFFu : (valid <= 0 ? 0u : ((1u << valid) - 1u));
 }
 
-// Delta[row] = sum_d dO[row, d] * O[row, d] in FP32; 8 threads per row, one
+// Delta[row] = sum_d dO[row, d] * O[row, d] in FP32; D/8 threads per row, one
 // 16-byte load of each operand per thread.
-template <bool BF16>
+template <int D, bool BF16>
 __global__ void __launch_bounds__(256) bwd_delta_kernel(const uint4* __restrict__ dout, const uint4* __restrict__ out,
                                                          float* __restrict__ delta, int64_t rows) {
+  constexpr int kPerRow = D / 8;
   const int64_t gid = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
-  const int64_t row = gid >> 3;
+  const int64_t row = gid / kPerRow;
   float acc = 0.f;
   if (row < rows) {
     const uint4 a = __ldg(dout + gid), b = __ldg(out + gid);
@@ -134,10 +150,9 @@ __global__ void __launch_bounds__(256) bwd_delta_kernel(const uint4* __restrict_
       acc = fmaf(x.y, y.y, acc);
     }
   }
-  acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-  acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-  acc += __shfl_xor_sync(0xffffffffu, acc, 4);
-  if (row < rows && (threadIdx.x & 7) == 0) delta[row] = acc;
+#pragma unroll
+  for (int o = 1; o < kPerRow; o <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+  if (row < rows && (threadIdx.x % kPerRow) == 0) delta[row] = acc;
 }
 
 // dq[i] = acc[i] in the input dtype, 8 elements per thread.
@@ -150,7 +165,7 @@ __global__ void __launch_bounds__(256) bwd_dq_convert_kernel(const float4* __res
   dq[i] = make_uint4(pack2<BF16>(a.x, a.y), pack2<BF16>(a.z, a.w), pack2<BF16>(b.x, b.y), pack2<BF16>(b.z, b.w));
 }
 
-template <bool BF16>
+template <int D, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
@@ -158,18 +173,21 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const float* __restrict__ delta, float* __restrict__ dq_acc, uint16_t* __restrict__ dk,
                     uint16_t* __restrict__ dv, int N, int W, int KT, int QT, int vec, float scale,
                     uint32_t* err_word, uint64_t timeout_ns) {
+  using C = BwdCfg<D>;
+  constexpr int kQBufs = C::kQBufs;
+  constexpr int kTileBytes = C::kTileBytes;
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t base = smem_u32(smem);
   if ((base & 1023u) != 0u) {
     if (threadIdx.x == 0) atomicOr(err_word, kDevErrLayout);
     return;
   }
-  BwdCtl& ctl = *reinterpret_cast<BwdCtl*>(smem + kOffCtl);
+  BwdCtl& ctl = *reinterpret_cast<BwdCtl*>(smem + C::kOffCtl);
   // Per buffer b: word w of query row i at s_mask[b * 4 * kT + w * kT + i];
   // LSE * log2(e) and Delta per query row at s_lse / s_delta [b * kT + i].
-  uint32_t* s_mask = reinterpret_cast<uint32_t*>(smem + kOffMask);
-  float* s_lse = reinterpret_cast<float*>(smem + kOffLse);
-  float* s_delta = reinterpret_cast<float*>(smem + kOffDelta);
+  uint32_t* s_mask = reinterpret_cast<uint32_t*>(smem + C::kOffMask);
+  float* s_lse = reinterpret_cast<float*>(smem + C::kOffLse);
+  float* s_delta = reinterpret_cast<float*>(smem + C::kOffDelta);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int bh = static_cast<int>(blockIdx.x) / KT;
@@ -215,17 +233,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tm_v);
       tma_prefetch_desc(&tm_do);
       mbar_arrive_expect_tx(smem_u32(&ctl.kv_full), 2 * kTileBytes);
-      tma_load_3d(base + kOffK, &tm_k, smem_u32(&ctl.kv_full), 0, k0, bh);
-      tma_load_3d(base + kOffV, &tm_v, smem_u32(&ctl.kv_full), 0, k0, bh);
+#pragma unroll
+      for (int dc = 0; dc < C::kDChunks; ++dc) {
+        tma_load_3d(base + C::kOffK + dc * kT * 128, &tm_k, smem_u32(&ctl.kv_full), dc * 64, k0, bh);
+        tma_load_3d(base + C::kOffV + dc * kT * 128, &tm_v, smem_u32(&ctl.kv_full), dc * 64, k0, bh);
+      }
     }
     bool ok = true;
     int last_copy = -1;  // last query tile whose Q/dO copies were started
     for (int qi = 0; qi < QT; ++qi) {
-      const int b = qi & 1;
+      const int b = qi % kQBufs;
       // Buffer b is free once the compute warps and the MMA issuer are done
-      // with tile qi-2 (its MMAs have completed by then).
-      if (qi >= 2 && !__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&ctl.tile_free[b]), ((qi - 2) >> 1) & 1,
-                                                                 abort_flag, timeout_ns))) {
+      // with tile qi-kQBufs (its MMAs have completed by then).
+      if (qi >= kQBufs &&
+          !__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&ctl.tile_free[b]), ((qi - kQBufs) / kQBufs) & 1,
+                                                     abort_flag, timeout_ns))) {
         ok = false;
         break;
       }
@@ -270,8 +292,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         ctl.live[b] = live ? 1u : 0u;
         if (live) {
           mbar_arrive_expect_tx(smem_u32(&ctl.ld_full[b]), 2 * kTileBytes);
-          tma_load_3d(base + kOffQ + b * kTileBytes, &tm_q, smem_u32(&ctl.ld_full[b]), 0, i0, bh);
-          tma_load_3d(base + kOffDO + b * kTileBytes, &tm_do, smem_u32(&ctl.ld_full[b]), 0, i0, bh);
+#pragma unroll
+          for (int dc = 0; dc < C::kDChunks; ++dc) {
+            tma_load_3d(base + C::kOffQ + b * kTileBytes + dc * kT * 128, &tm_q, smem_u32(&ctl.ld_full[b]), dc * 64,
+                        i0, bh);
+            tma_load_3d(base + C::kOffDO + b * kTileBytes + dc * kT * 128, &tm_do, smem_u32(&ctl.ld_full[b]),
+                        dc * 64, i0, bh);
+          }
           last_copy = qi;
         } else {
           mbar_arrive(smem_u32(&ctl.ld_full[b]));
@@ -283,38 +310,43 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Let the copies this warp started land before the CTA exits.
       uint32_t zero = 0;
       mbar_wait_bounded(smem_u32(&ctl.kv_full), 0, &zero, timeout_ns);
-      for (int qi = last_copy - 1; qi <= last_copy; ++qi)
-        if (qi >= 0) mbar_wait_bounded(smem_u32(&ctl.ld_full[qi & 1]), (qi >> 1) & 1, &zero, timeout_ns);
+      for (int qi = last_copy - kQBufs + 1; qi <= last_copy; ++qi)
+        if (qi >= 0) mbar_wait_bounded(smem_u32(&ctl.ld_full[qi % kQBufs]), (qi / kQBufs) & 1, &zero, timeout_ns);
     }
   } else if (warp == 5) {
     // ================================================================ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_f16(kT, kT, BF16 ? 1 : 0, 0);       // S^T, dP^T (M = keys)
-      constexpr uint32_t idesc_kv = make_idesc_f16(kT, kD, BF16 ? 1 : 0, 1);      // dV, dK (B M/N-major)
-      constexpr uint32_t idesc_q = make_idesc_f16(kT, kD, BF16 ? 1 : 0, 1, 1);    // dQ (A and B M/N-major)
-      const uint32_t sK = base + kOffK, sV = base + kOffV, sDS = base + kOffDS;
+      constexpr uint32_t idesc_kv = make_idesc_f16(kT, D, BF16 ? 1 : 0, 1);       // dV, dK (B M/N-major)
+      constexpr uint32_t idesc_q = make_idesc_f16(kT, 64, BF16 ? 1 : 0, 1, 1);    // dQ half (A and B M/N-major)
+      const uint32_t sK = base + C::kOffK, sV = base + C::kOffV, sDS = base + C::kOffDS;
       bool ok = mbar_wait_bounded(smem_u32(&ctl.kv_full), 0, abort_flag, timeout_ns);
       uint32_t lt = 0;  // live query tiles done
       for (int qi = 0; ok && qi < QT; ++qi) {
-        const int b = qi & 1;
-        const uint32_t sQ = base + kOffQ + b * kTileBytes, sDO = base + kOffDO + b * kTileBytes;
+        const int b = qi % kQBufs;
+        const uint32_t sQ = base + C::kOffQ + b * kTileBytes, sDO = base + C::kOffDO + b * kTileBytes;
         // Tile qi's staging, and tile qi-1 finished (its TMEM results read).
-        if (!mbar_wait_bounded(smem_u32(&ctl.ld_full[b]), (qi >> 1) & 1, abort_flag, timeout_ns) ||
-            (qi > 0 && !mbar_wait_bounded(smem_u32(&ctl.tile_free[b ^ 1]), ((qi - 1) >> 1) & 1, abort_flag,
-                                          timeout_ns))) {
+        if (!mbar_wait_bounded(smem_u32(&ctl.ld_full[b]), (qi / kQBufs) & 1, abort_flag, timeout_ns) ||
+            (qi > 0 && !mbar_wait_bounded(smem_u32(&ctl.tile_free[(qi - 1) % kQBufs]), ((qi - 1) / kQBufs) & 1,
+                                          abort_flag, timeout_ns))) {
           ok = false;
           break;
         }
         if (ctl.live[b] != 0u) {
           tc_fence_after();
+          // 16 head dims per step: swizzle chunk kk/4 of the rows, 32 bytes into it.
 #pragma unroll
-          for (int kk = 0; kk < kD / 16; ++kk)
-            mma_ss(tmem + kColS, smem_desc_sw128(sK + kk * 32, 16, 1024), smem_desc_sw128(sQ + kk * 32, 16, 1024),
-                   idesc_s, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * (kT * 128) + (kk & 3) * 32;
+            mma_ss(tmem + kColS, smem_desc_sw128(sK + off, 16, 1024), smem_desc_sw128(sQ + off, 16, 1024), idesc_s,
+                   kk > 0 ? 1u : 0u);
+          }
 #pragma unroll
-          for (int kk = 0; kk < kD / 16; ++kk)
-            mma_ss(tmem + kColDP, smem_desc_sw128(sV + kk * 32, 16, 1024),
-                   smem_desc_sw128(sDO + kk * 32, 16, 1024), idesc_s, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * (kT * 128) + (kk & 3) * 32;
+            mma_ss(tmem + kColDP, smem_desc_sw128(sV + off, 16, 1024), smem_desc_sw128(sDO + off, 16, 1024), idesc_s,
+                   kk > 0 ? 1u : 0u);
+          }
           mma_commit(smem_u32(&ctl.st_full));
           if (!mbar_wait_bounded(smem_u32(&ctl.p_full), lt & 1, abort_flag, timeout_ns)) {
             ok = false;
@@ -322,21 +354,24 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           tc_fence_after();
           // 16 query rows per step: 8 packed TMEM columns of P^T / dS^T, 2048
-          // bytes (16 rows of 128) into the M/N-major shared-memory operands.
+          // bytes (16 rows of 128) into the M/N-major shared-memory operands,
+          // whose 64-dim chunks (D = 128) are kT * 128 bytes apart.
 #pragma unroll
           for (int kk = 0; kk < kT / 16; ++kk)
             mma_ts(tmem + kColDV, tmem + kColS + kk * 8, smem_desc_sw128(sDO + kk * 2048, kT * 128, 1024),
                    idesc_kv, (lt > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
           for (int kk = 0; kk < kT / 16; ++kk)
-            mma_ts(tmem + kColDK, tmem + kColDP + kk * 8, smem_desc_sw128(sQ + kk * 2048, kT * 128, 1024),
+            mma_ts(tmem + C::kColDK, tmem + kColDP + kk * 8, smem_desc_sw128(sQ + kk * 2048, kT * 128, 1024),
                    idesc_kv, (lt > 0 || kk > 0) ? 1u : 0u);
-          // dQ_part = dS K: 16 keys per step; dS's two 64-query chunks are
-          // kT * 128 bytes apart.
+          // dQ_part = dS K in 64-dim halves: 16 keys per step; dS's two
+          // 64-query chunks are kT * 128 bytes apart, as are K's 64-dim chunks.
 #pragma unroll
-          for (int kk = 0; kk < kT / 16; ++kk)
-            mma_ss(tmem + kColDQ, smem_desc_sw128(sDS + kk * 2048, kT * 128, 1024),
-                   smem_desc_sw128(sK + kk * 2048, kT * 128, 1024), idesc_q, kk > 0 ? 1u : 0u);
+          for (int h = 0; h < C::kDChunks; ++h)
+#pragma unroll
+            for (int kk = 0; kk < kT / 16; ++kk)
+              mma_ss(tmem + C::col_dq(h), smem_desc_sw128(sDS + kk * 2048, kT * 128, 1024),
+                     smem_desc_sw128(sK + h * (kT * 128) + kk * 2048, kT * 128, 1024), idesc_q, kk > 0 ? 1u : 0u);
           mma_commit(smem_u32(&ctl.dq_full));
           ++lt;
         }
@@ -369,11 +404,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive(smem_u32(&bar));
     };
     for (int qi = 0; qi < QT; ++qi) {
-      const int b = qi & 1;
+      const int b = qi % kQBufs;
       const uint32_t* my_words = s_mask + b * 4 * kT + my_word;
       const float* t_lse = s_lse + b * kT;
       const float* t_delta = s_delta + b * kT;
-      if (ok) ok = wait_all(ctl.ld_full[b], (qi >> 1) & 1);
+      if (ok) ok = wait_all(ctl.ld_full[b], (qi / kQBufs) & 1);
       if (ok && ctl.live[b] != 0u) {
         ok = wait_all(ctl.st_full, lt & 1);
         if (ok) {
@@ -409,7 +444,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             // dS for the dQ MMA: row t of the M-major operand, queries
             // 32c .. 32c+31 = 16-byte chunks 4(c&1) .. +3 of 64-query chunk c/2,
             // 128-byte swizzle (chunk index XOR row % 8).
-            uint8_t* drow = smem + kOffDS + (c >> 1) * kTileBytes + t * 128;
+            uint8_t* drow = smem + C::kOffDS + (c >> 1) * (kT * 128) + t * 128;
 #pragma unroll
             for (int j = 0; j < 4; ++j)
               *reinterpret_cast<uint4*>(drow + ((((c & 1) * 4 + j) ^ (t & 7)) * 16)) =
@@ -423,12 +458,12 @@ __global__ void __launch_bounds__(kThreads, 1)
             // dQ_part row t = query row qi*128 + t, scaled, added into the accumulator.
             const int row = qi * kT + t;
 #pragma unroll 1
-            for (int h = 0; h < 2; ++h) {
+            for (int h = 0; h < D / 32; ++h) {
               uint32_t u[32];
-              tmem_ld32(t_lane + kColDQ + h * 32, u);
+              tmem_ld32(t_lane + C::col_dq(h >> 1) + (h & 1) * 32, u);
               tmem_wait_ld();
               if (row < N) {
-                float* dst = dq_acc + (static_cast<int64_t>(bh) * N + row) * kD + h * 32;
+                float* dst = dq_acc + (static_cast<int64_t>(bh) * N + row) * D + h * 32;
 #pragma unroll
                 for (int q4 = 0; q4 < 8; ++q4)
                   red_add_v4(dst + 4 * q4, __uint_as_float(u[4 * q4]) * scale, __uint_as_float(u[4 * q4 + 1]) * scale,
@@ -444,7 +479,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // dV and dK of this key tile (lane t = key k0 + t); zero when no query tile was live.
     const int key = k0 + t;
 #pragma unroll 1
-    for (int h = 0; h < 2; ++h) {
+    for (int h = 0; h < D / 32; ++h) {
       uint32_t vw[16], kw[16];
       if (ok && lt > 0) {
         uint32_t u[32];
@@ -452,7 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tmem_wait_ld();
 #pragma unroll
         for (int e = 0; e < 16; ++e) vw[e] = pack2<BF16>(__uint_as_float(u[2 * e]), __uint_as_float(u[2 * e + 1]));
-        tmem_ld32(t_lane + kColDK + h * 32, u);
+        tmem_ld32(t_lane + C::kColDK + h * 32, u);
         tmem_wait_ld();
 #pragma unroll
         for (int e = 0; e < 16; ++e)
@@ -462,8 +497,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int e = 0; e < 16; ++e) vw[e] = kw[e] = 0u;
       }
       if (key < N && ctl.abort_flag == 0) {
-        uint4* dvr = reinterpret_cast<uint4*>(dv + (static_cast<int64_t>(bh) * N + key) * kD + h * 32);
-        uint4* dkr = reinterpret_cast<uint4*>(dk + (static_cast<int64_t>(bh) * N + key) * kD + h * 32);
+        uint4* dvr = reinterpret_cast<uint4*>(dv + (static_cast<int64_t>(bh) * N + key) * D + h * 32);
+        uint4* dkr = reinterpret_cast<uint4*>(dk + (static_cast<int64_t>(bh) * N + key) * D + h * 32);
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           dvr[q] = make_uint4(vw[4 * q], vw[4 * q + 1], vw[4 * q + 2], vw[4 * q + 3]);
@@ -482,8 +517,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-template <bool BF16>
+template <int D, bool BF16>
 int launch(const BwdParams& p, const char** msg) {
+  using C = BwdCfg<D>;
   const int64_t BH = p.B * p.H;
   const int64_t N = p.N;
   const int64_t W = (N + 31) / 32;
@@ -494,9 +530,8 @@ int launch(const BwdParams& p, const char** msg) {
     return kErrArg;
   }
   CUtensorMap mq, mk, mv, mdo;
-  if (!make_tensor_map_3d(&mq, p.q, p.dtype, kD, BH, N, kT) || !make_tensor_map_3d(&mk, p.k, p.dtype, kD, BH, N, kT) ||
-      !make_tensor_map_3d(&mv, p.v, p.dtype, kD, BH, N, kT) ||
-      !make_tensor_map_3d(&mdo, p.dout, p.dtype, kD, BH, N, kT)) {
+  if (!make_tensor_map_3d(&mq, p.q, p.dtype, D, BH, N, kT) || !make_tensor_map_3d(&mk, p.k, p.dtype, D, BH, N, kT) ||
+      !make_tensor_map_3d(&mv, p.v, p.dtype, D, BH, N, kT) || !make_tensor_map_3d(&mdo, p.dout, p.dtype, D, BH, N, kT)) {
     *msg = "backward: cuTensorMapEncodeTiled failed (pointer alignment or driver entry point)";
     return kErrCuda;
   }
@@ -506,9 +541,10 @@ int launch(const BwdParams& p, const char** msg) {
     return kErrCuda;
   }
   static bool smem_set[kMaxDevices] = {};
-  auto kern = attn_bwd_kernel<BF16>;
+  auto kern = attn_bwd_kernel<D, BF16>;
   if (!smem_set[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+    cudaError_t e =
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::kSmemBytes));
     if (e != cudaSuccess) {
       *msg = cudaGetErrorString(e);
       return kErrLaunch;
@@ -516,22 +552,22 @@ int launch(const BwdParams& p, const char** msg) {
     smem_set[dev] = true;
   }
   const int64_t rows = BH * N;
-  cudaError_t e = cudaMemsetAsync(p.dq_accum, 0, static_cast<size_t>(rows) * kD * sizeof(float), p.stream);
+  cudaError_t e = cudaMemsetAsync(p.dq_accum, 0, static_cast<size_t>(rows) * D * sizeof(float), p.stream);
   if (e == cudaSuccess) {
-    bwd_delta_kernel<BF16><<<static_cast<unsigned>((rows * 8 + 255) / 256), 256, 0, p.stream>>>(
+    bwd_delta_kernel<D, BF16><<<static_cast<unsigned>((rows * (D / 8) + 255) / 256), 256, 0, p.stream>>>(
         static_cast<const uint4*>(p.dout), static_cast<const uint4*>(p.out), p.delta, rows);
     e = cudaGetLastError();
   }
   if (e == cudaSuccess) {
     const int vec = (W % 4 == 0 && (reinterpret_cast<uintptr_t>(p.mask) & 15u) == 0) ? 1 : 0;
-    kern<<<static_cast<unsigned>(BH * KT), kThreads, kSmemBytes, p.stream>>>(
+    kern<<<static_cast<unsigned>(BH * KT), kThreads, C::kSmemBytes, p.stream>>>(
         mq, mk, mv, mdo, p.mask, p.lse, p.delta, p.dq_accum, static_cast<uint16_t*>(p.dk),
         static_cast<uint16_t*>(p.dv), static_cast<int>(N), static_cast<int>(W), static_cast<int>(KT),
         static_cast<int>(QT), vec, p.scale, p.err_word, p.timeout_ns);
     e = cudaGetLastError();
   }
   if (e == cudaSuccess) {
-    const int64_t n8 = rows * kD / 8;
+    const int64_t n8 = rows * D / 8;
     bwd_dq_convert_kernel<BF16><<<static_cast<unsigned>((n8 + 255) / 256), 256, 0, p.stream>>>(
         reinterpret_cast<const float4*>(p.dq_accum), static_cast<uint4*>(p.dq), n8);
     e = cudaGetLastError();
@@ -546,15 +582,16 @@ int launch(const BwdParams& p, const char** msg) {
 }  // namespace
 
 int launch_attn_bwd(const BwdParams& p, const char** msg) {
-  if (p.D != kD) {
-    *msg = "backward: head dim must be 64";
+  if (p.D != 64 && p.D != 128) {
+    *msg = "backward: head dim must be 64 or 128";
     return kErrUnsupportedD;
   }
   if (p.N > kMaxSeqLen) {
     *msg = "backward: sequence length above the supported maximum (65536)";
     return kErrUnsupportedN;
   }
-  return p.dtype == 1 ? launch<true>(p, msg) : launch<false>(p, msg);
+  if (p.D == 128) return p.dtype == 1 ? launch<128, true>(p, msg) : launch<128, false>(p, msg);
+  return p.dtype == 1 ? launch<64, true>(p, msg) : launch<64, false>(p, msg);
 }
 
 }  // namespace sma

@@ -172,7 +172,7 @@ int sma_attn_bwd(int dtype, const void* q, const void* k, const void* v, const v
   if (dtype != SMA_DTYPE_FP16 && dtype != SMA_DTYPE_BF16)
     return fail(sma::kErrDtype, "backward: unsupported dtype, need fp16 or bf16");
   if (B < 0 || H < 0 || N < 0 || D <= 0) return fail(sma::kErrArg, "backward: bad dimension");
-  if (D != 64) return fail(sma::kErrUnsupportedD, "backward: head dim must be 64");
+  if (D != 64 && D != 128) return fail(sma::kErrUnsupportedD, "backward: head dim must be 64 or 128");
   if (N > SMA_MAX_SEQ_LEN) return fail(sma::kErrUnsupportedN, "backward: sequence length above the supported maximum (65536)");
   if (!(scale > 0.f) || !(scale < INFINITY)) return fail(sma::kErrArg, "backward: scale must be finite and > 0");
   if (B == 0 || H == 0 || N == 0) return sma::kOk;

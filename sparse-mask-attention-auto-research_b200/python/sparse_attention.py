@@ -18,9 +18,9 @@ Differences from the reference, all deliberate:
     RuntimeError (the FP32 reference lives in the test oracle, not here).
   * ``sparse_attention_func`` works (the reference passes lse=None to a
     binding that rejects it).
-  * ``SparseAttentionFunction.backward`` runs the backward kernel (head dim
-    64); the reference's CUDA backward is an unbound stub (AttributeError
-    when called) and its CPU formulas define the result.
+  * ``SparseAttentionFunction.backward`` runs the backward kernel; the
+    reference's CUDA backward is an unbound stub (AttributeError when
+    called) and its CPU formulas define the result.
   * ``sparse_attention`` / ``sparse_attention_func`` pack long or large
     masks with the fused packer, which also writes the per-query-tile map of
     live key tiles the attention kernel then uses (same results, no

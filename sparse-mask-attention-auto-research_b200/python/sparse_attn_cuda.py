@@ -110,7 +110,7 @@ def backward(dout, q, k, v, out, lse, mask_packed, dq, dk, dv, scale):
     """Sparse attention backward with the signature the reference calls
     (python/sparse_attention.py:93-96; never bound by its csrc/binding.cpp).
     Writes dq, dk, dv (shape and dtype of q) from the forward's out and lse.
-    Head dim 64 only; the FP32 scratch it needs is allocated here."""
+    Head dims 64 and 128; the FP32 scratch it needs is allocated here."""
     _require(q.is_cuda, "q must be CUDA tensor")
     _require(q.dim() == 4, "q must be 4D")
     _require(q.dtype in _DTYPES, "Unsupported dtype, need BF16 or FP16")

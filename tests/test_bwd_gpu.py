@@ -53,10 +53,7 @@ def check_grads(got, want, dtype, mask):
     assert torch.all(got[2].float().cpu()[empty_cols] == 0), "keys no row attends get dv = 0"
 
 
-D64 = [p for p in golden_paths("bwd") if "D128" not in p]
-
-
-@pytest.mark.parametrize("path", D64, ids=[i for i in golden_ids("bwd") if "D128" not in i])
+@pytest.mark.parametrize("path", golden_paths("bwd"), ids=golden_ids("bwd"))
 def test_golden(path):
     case = load_golden(path)
     q, k, v, dout, m = (case[x].to(DEV) for x in ("q", "k", "v", "dout", "mask"))
@@ -64,7 +61,8 @@ def test_golden(path):
     check_grads(got, (case["dq"], case["dk"], case["dv"]), case["dtype"], case["mask"])
 
 
-@pytest.mark.parametrize("name,kw", [("c1", dict(B=2)), ("c4", dict(B=1, H=2)), ("c2", dict(B=4, dtype=torch.bfloat16))])
+@pytest.mark.parametrize("name,kw", [("c1", dict(B=2)), ("c4", dict(B=1, H=2)), ("c2", dict(B=4, dtype=torch.bfloat16)),
+                                     ("c3", dict(B=1, H=2)), ("c3", dict(B=1, H=1, N=700, dtype=torch.float16))])
 def test_workload_vs_oracle(name, kw):
     q, k, v, m = workloads.make_inputs(name, seed=11, device=DEV, **kw)
     g = torch.Generator(device=DEV).manual_seed(12)
@@ -86,6 +84,18 @@ def test_autograd_through_public_api():
     (out.float() * w.float()).sum().backward()
     want = oracle.attention_backward(*(x.detach().float().cpu().numpy() for x in (q, k, v)), m.cpu().numpy(),
                                      1 / math.sqrt(q.shape[-1]), w.float().cpu().numpy())
+    check_grads((q.grad, k.grad, v.grad), want, q.dtype, m.cpu())
+
+
+def test_autograd_head_dim_128():
+    q, k, v, m = workloads.make_inputs("c3", seed=18, device=DEV, B=1, H=2)
+    q, k, v = (x.clone().requires_grad_(True) for x in (q, k, v))
+    g = torch.Generator(device=DEV).manual_seed(19)
+    w = torch.randn(q.shape, generator=g, device=DEV).to(q.dtype)
+    out = sparse_attention(q, k, v, m)
+    (out.float() * w.float()).sum().backward()
+    want = oracle.attention_backward(*(x.detach().float().cpu().numpy() for x in (q, k, v)), m.cpu().numpy(),
+                                     1 / math.sqrt(128), w.float().cpu().numpy())
     check_grads((q.grad, k.grad, v.grad), want, q.dtype, m.cpu())
 
 
