@@ -12,8 +12,9 @@
 //
 // Kernels (one stream, in order):
 //   bwd_delta_kernel   Delta from dO and O (FP32), 8 threads per row
-//   attn_bwd_kernel    one CTA per (batch*head, 128-key tile).  K and V stay
-//                      in shared memory, dK and dV accumulate in TMEM, and the
+//   attn_bwd_kernel    persistent, one CTA per SM looping over the items
+//                      (batch*head, 128-key tile).  Per item K and V stay in
+//                      shared memory, dK and dV accumulate in TMEM, and the
 //                      CTA walks the 128-row query tiles whose mask block with
 //                      its key tile has a set bit.  Per live query tile:
 //                        MMA  S^T = K Q^T, dP^T = V dO^T   (M = keys)
@@ -48,8 +49,9 @@ constexpr float kLog2e = 1.44269504088896340736f;
 constexpr int kMaxDevices = 64;
 
 // Per head dim.  Tiles of K, V, Q, dO are kT rows of D/64 128-byte swizzle
-// chunks.  D = 64 stages query tiles in two buffers (the loader fills tile
-// i+1 while tile i is computed); D = 128 has shared memory for one.
+// chunks.  D = 64 double-buffers K/V (the next item's keys load while the
+// current item computes) and the query tiles (the loader fills tile i+1 while
+// tile i is computed); D = 128 has shared memory for one of each.
 // TMEM: S^T [0,128) and dP^T [128,256) (P^T / dS^T packed over their first
 // 64 columns), dV [256, 256+D), dK [256+D, 256+2D); dQ_part in 64-column
 // halves: D = 64 at [384,448), D = 128 over the S^T / dP^T columns that
@@ -59,12 +61,16 @@ struct BwdCfg {
   static_assert(D == 64 || D == 128, "head dim");
   static constexpr int kDChunks = D / 64;
   static constexpr int kTileBytes = kT * D * 2;  // 16 / 32 KiB
+  static constexpr int kKVBufs = D == 64 ? 2 : 1;
   static constexpr int kQBufs = D == 64 ? 2 : 1;
   static constexpr uint32_t kColDK = kColDV + D;
   __host__ __device__ static constexpr uint32_t col_dq(int h) { return D == 64 ? 384u : (h == 0 ? 64u : 192u); }
+  // The next tile's S^T / dP^T may be issued while the compute warps still
+  // read this tile's dQ_part only when the two do not share TMEM columns.
+  static constexpr bool kDQApart = D == 64;
   static constexpr int kOffK = 0;
-  static constexpr int kOffV = kTileBytes;
-  static constexpr int kOffQ = 2 * kTileBytes;
+  static constexpr int kOffV = kKVBufs * kTileBytes;
+  static constexpr int kOffQ = 2 * kKVBufs * kTileBytes;
   static constexpr int kOffDO = kOffQ + kQBufs * kTileBytes;
   static constexpr int kOffDS = kOffDO + kQBufs * kTileBytes;  // two 16 KiB M-major chunks of 64 queries
   static constexpr int kOffMask = kOffDS + 2 * kT * 128;
@@ -73,11 +79,13 @@ struct BwdCfg {
   static constexpr int kOffCtl = kOffDelta + kQBufs * kT * 4;
   // Above half of the SM's shared memory, so one CTA holds an SM (its TMEM
   // allocation takes all 512 columns).
-  static constexpr size_t kSmemBytes = D == 64 ? 136 * 1024 : 168 * 1024;
+  static constexpr size_t kSmemBytes = 168 * 1024;
 };
 
 struct BwdCtl {
-  uint64_t kv_full;       // K and V landed
+  uint64_t kv_full[2];    // K and V of an item landed in buffer b
+  uint64_t kv_free[2];    // MMAs of the item in K/V buffer b complete (committed by the MMA issuer)
+  uint64_t acc_free;      // dV and dK of an item read out of TMEM (4 compute warps)
   uint64_t ld_full[2];    // query tile staged in buffer b (Q, dO by TMA; mask, LSE, Delta by the loader warp)
   uint64_t st_full;       // S^T and dP^T complete
   uint64_t p_full;        // P^T, dS^T in TMEM and dS in shared memory (4 compute warps)
@@ -89,8 +97,8 @@ struct BwdCtl {
   uint32_t abort_flag;
 };
 
-// Shared memory: K | V | Q[kQBufs] | dO[kQBufs] | dS | mask words
-// [kQBufs][4][128] | lse2 [kQBufs][128] | Delta [kQBufs][128] | control.
+// Shared memory: K[kKVBufs] | V[kKVBufs] | Q[kQBufs] | dO[kQBufs] | dS | mask
+// words [kQBufs][4][128] | lse2 [kQBufs][128] | Delta [kQBufs][128] | control.
 static_assert(BwdCfg<64>::kOffCtl + sizeof(BwdCtl) <= BwdCfg<64>::kSmemBytes, "shared memory layout");
 static_assert(BwdCfg<128>::kOffCtl + sizeof(BwdCtl) <= BwdCfg<128>::kSmemBytes, "shared memory layout");
 
@@ -171,10 +179,11 @@ __global__ void __launch_bounds__(kThreads, 1)
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                     const uint32_t* __restrict__ mask, const float* __restrict__ lse,
                     const float* __restrict__ delta, float* __restrict__ dq_acc, uint16_t* __restrict__ dk,
-                    uint16_t* __restrict__ dv, int N, int W, int KT, int QT, int vec, float scale,
+                    uint16_t* __restrict__ dv, int N, int W, int KT, int QT, int total_items, int vec, float scale,
                     uint32_t* err_word, uint64_t timeout_ns) {
   using C = BwdCfg<D>;
   constexpr int kQBufs = C::kQBufs;
+  constexpr int kKVBufs = C::kKVBufs;
   constexpr int kTileBytes = C::kTileBytes;
   extern __shared__ __align__(1024) uint8_t smem[];
   const uint32_t base = smem_u32(smem);
@@ -190,21 +199,27 @@ __global__ void __launch_bounds__(kThreads, 1)
   float* s_delta = reinterpret_cast<float*>(smem + C::kOffDelta);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int bh = static_cast<int>(blockIdx.x) / KT;
-  const int kt = static_cast<int>(blockIdx.x) - bh * KT;
-  const int k0 = kt * kT;
+  // Persistent: CTA c takes items c, c + G, c + 2G, ... of item = batch*head *
+  // KT + key tile, so the CTAs running at one time cover the key tiles of a
+  // few heads side by side and share those heads' Q and dO in L2.  Counters
+  // that run over all items of the CTA: j (items; K/V buffer j % kKVBufs), gq
+  // (query tiles; staging buffer gq % kQBufs), lt (live query tiles).
+  const int G = static_cast<int>(gridDim.x);
+  const int n_items = (total_items - static_cast<int>(blockIdx.x) + G - 1) / G;
   volatile uint32_t* abort_flag = &ctl.abort_flag;
 
   if (threadIdx.x == 128) {
-    mbar_init(smem_u32(&ctl.kv_full), 1);
-    mbar_init(smem_u32(&ctl.st_full), 1);
-    mbar_init(smem_u32(&ctl.p_full), 4);
-    mbar_init(smem_u32(&ctl.dq_full), 1);
     for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&ctl.kv_full[b]), 1);
+      mbar_init(smem_u32(&ctl.kv_free[b]), 1);
       mbar_init(smem_u32(&ctl.ld_full[b]), 1);
       mbar_init(smem_u32(&ctl.tile_free[b]), 5);  // 4 compute warps + the MMA issuer
       ctl.live[b] = 0;
     }
+    mbar_init(smem_u32(&ctl.acc_free), 4);
+    mbar_init(smem_u32(&ctl.st_full), 1);
+    mbar_init(smem_u32(&ctl.p_full), 4);
+    mbar_init(smem_u32(&ctl.dq_full), 1);
     mbar_init(smem_u32(&ctl.drain), 1);
     ctl.abort_flag = 0;
     fence_barrier_init();
@@ -232,76 +247,96 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       tma_prefetch_desc(&tm_do);
-      mbar_arrive_expect_tx(smem_u32(&ctl.kv_full), 2 * kTileBytes);
-#pragma unroll
-      for (int dc = 0; dc < C::kDChunks; ++dc) {
-        tma_load_3d(base + C::kOffK + dc * kT * 128, &tm_k, smem_u32(&ctl.kv_full), dc * 64, k0, bh);
-        tma_load_3d(base + C::kOffV + dc * kT * 128, &tm_v, smem_u32(&ctl.kv_full), dc * 64, k0, bh);
-      }
     }
     bool ok = true;
-    int last_copy = -1;  // last query tile whose Q/dO copies were started
-    for (int qi = 0; qi < QT; ++qi) {
-      const int b = qi % kQBufs;
-      // Buffer b is free once the compute warps and the MMA issuer are done
-      // with tile qi-kQBufs (its MMAs have completed by then).
-      if (qi >= kQBufs &&
-          !__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&ctl.tile_free[b]), ((qi - kQBufs) / kQBufs) & 1,
+    int gq = 0;
+    int last_copy = -1;  // last query tile (in gq) whose Q/dO copies were started
+    int kv_copies = 0;   // items whose K/V copies were started
+    for (int j = 0; ok && j < n_items; ++j) {
+      const int item = static_cast<int>(blockIdx.x) + j * G;
+      const int bh = item / KT;
+      const int kt = item - bh * KT;
+      const int bkv = j % kKVBufs;
+      // K/V buffer bkv is free once the MMAs of item j - kKVBufs are complete.
+      if (j >= kKVBufs &&
+          !__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&ctl.kv_free[bkv]), ((j - kKVBufs) / kKVBufs) & 1,
                                                      abort_flag, timeout_ns))) {
         ok = false;
         break;
       }
-      const int i0 = qi * kT;
-      uint32_t any = 0u;
-#pragma unroll
-      for (int rr = 0; rr < 4; ++rr) {
-        const int i = lane + 32 * rr;
-        const int row = i0 + i;
-        uint32_t w4[4] = {0u, 0u, 0u, 0u};
-        float l2 = 0.f, de = 0.f;
-        if (row < N) {
-          const uint32_t* mrow = mask + (static_cast<int64_t>(bh) * N + row) * W + kt * 4;
-          if (vec) {
-            const uint4 x = __ldg(reinterpret_cast<const uint4*>(mrow));
-            w4[0] = x.x;
-            w4[1] = x.y;
-            w4[2] = x.z;
-            w4[3] = x.w;
-          } else {
-#pragma unroll
-            for (int w = 0; w < 4; ++w) w4[w] = (kt * 4 + w < W) ? __ldg(mrow + w) : 0u;
-          }
-#pragma unroll
-          for (int w = 0; w < 4; ++w) w4[w] &= valid_bits(kt * 4 + w, N);
-          // -FLT_MAX (a row with no kept key) becomes -inf; such a row has no
-          // mask bit, so its P is 0 by the select and never uses this value.
-          l2 = lse[static_cast<int64_t>(bh) * N + row] * kLog2e;
-          de = delta[static_cast<int64_t>(bh) * N + row];
-        }
-#pragma unroll
-        for (int w = 0; w < 4; ++w) {
-          s_mask[b * 4 * kT + w * kT + i] = w4[w];
-          any |= w4[w];
-        }
-        s_lse[b * kT + i] = l2;
-        s_delta[b * kT + i] = de;
-      }
-      const bool live = __any_sync(0xffffffffu, any != 0u);
-      __syncwarp();
       if (lane == 0) {
-        ctl.live[b] = live ? 1u : 0u;
-        if (live) {
-          mbar_arrive_expect_tx(smem_u32(&ctl.ld_full[b]), 2 * kTileBytes);
+        mbar_arrive_expect_tx(smem_u32(&ctl.kv_full[bkv]), 2 * kTileBytes);
 #pragma unroll
-          for (int dc = 0; dc < C::kDChunks; ++dc) {
-            tma_load_3d(base + C::kOffQ + b * kTileBytes + dc * kT * 128, &tm_q, smem_u32(&ctl.ld_full[b]), dc * 64,
-                        i0, bh);
-            tma_load_3d(base + C::kOffDO + b * kTileBytes + dc * kT * 128, &tm_do, smem_u32(&ctl.ld_full[b]),
-                        dc * 64, i0, bh);
+        for (int dc = 0; dc < C::kDChunks; ++dc) {
+          tma_load_3d(base + C::kOffK + bkv * kTileBytes + dc * kT * 128, &tm_k, smem_u32(&ctl.kv_full[bkv]),
+                      dc * 64, kt * kT, bh);
+          tma_load_3d(base + C::kOffV + bkv * kTileBytes + dc * kT * 128, &tm_v, smem_u32(&ctl.kv_full[bkv]),
+                      dc * 64, kt * kT, bh);
+        }
+      }
+      ++kv_copies;
+      for (int qi = 0; qi < QT; ++qi, ++gq) {
+        const int b = gq % kQBufs;
+        // Buffer b is free once the compute warps and the MMA issuer are done
+        // with tile gq - kQBufs (its MMAs have completed by then).
+        if (gq >= kQBufs &&
+            !__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&ctl.tile_free[b]), ((gq - kQBufs) / kQBufs) & 1,
+                                                       abort_flag, timeout_ns))) {
+          ok = false;
+          break;
+        }
+        const int i0 = qi * kT;
+        uint32_t any = 0u;
+#pragma unroll
+        for (int rr = 0; rr < 4; ++rr) {
+          const int i = lane + 32 * rr;
+          const int row = i0 + i;
+          uint32_t w4[4] = {0u, 0u, 0u, 0u};
+          float l2 = 0.f, de = 0.f;
+          if (row < N) {
+            const uint32_t* mrow = mask + (static_cast<int64_t>(bh) * N + row) * W + kt * 4;
+            if (vec) {
+              const uint4 x = __ldg(reinterpret_cast<const uint4*>(mrow));
+              w4[0] = x.x;
+              w4[1] = x.y;
+              w4[2] = x.z;
+              w4[3] = x.w;
+            } else {
+#pragma unroll
+              for (int w = 0; w < 4; ++w) w4[w] = (kt * 4 + w < W) ? __ldg(mrow + w) : 0u;
+            }
+#pragma unroll
+            for (int w = 0; w < 4; ++w) w4[w] &= valid_bits(kt * 4 + w, N);
+            // -FLT_MAX (a row with no kept key) becomes -inf; such a row has no
+            // mask bit, so its P is 0 by the select and never uses this value.
+            l2 = lse[static_cast<int64_t>(bh) * N + row] * kLog2e;
+            de = delta[static_cast<int64_t>(bh) * N + row];
           }
-          last_copy = qi;
-        } else {
-          mbar_arrive(smem_u32(&ctl.ld_full[b]));
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            s_mask[b * 4 * kT + w * kT + i] = w4[w];
+            any |= w4[w];
+          }
+          s_lse[b * kT + i] = l2;
+          s_delta[b * kT + i] = de;
+        }
+        const bool live = __any_sync(0xffffffffu, any != 0u);
+        __syncwarp();
+        if (lane == 0) {
+          ctl.live[b] = live ? 1u : 0u;
+          if (live) {
+            mbar_arrive_expect_tx(smem_u32(&ctl.ld_full[b]), 2 * kTileBytes);
+#pragma unroll
+            for (int dc = 0; dc < C::kDChunks; ++dc) {
+              tma_load_3d(base + C::kOffQ + b * kTileBytes + dc * kT * 128, &tm_q, smem_u32(&ctl.ld_full[b]),
+                          dc * 64, i0, bh);
+              tma_load_3d(base + C::kOffDO + b * kTileBytes + dc * kT * 128, &tm_do, smem_u32(&ctl.ld_full[b]),
+                          dc * 64, i0, bh);
+            }
+            last_copy = gq;
+          } else {
+            mbar_arrive(smem_u32(&ctl.ld_full[b]));
+          }
         }
       }
     }
@@ -309,9 +344,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       fail();
       // Let the copies this warp started land before the CTA exits.
       uint32_t zero = 0;
-      mbar_wait_bounded(smem_u32(&ctl.kv_full), 0, &zero, timeout_ns);
-      for (int qi = last_copy - kQBufs + 1; qi <= last_copy; ++qi)
-        if (qi >= 0) mbar_wait_bounded(smem_u32(&ctl.ld_full[qi % kQBufs]), (qi / kQBufs) & 1, &zero, timeout_ns);
+      for (int jj = kv_copies - kKVBufs; jj < kv_copies; ++jj)
+        if (jj >= 0) mbar_wait_bounded(smem_u32(&ctl.kv_full[jj % kKVBufs]), (jj / kKVBufs) & 1, &zero, timeout_ns);
+      for (int g = last_copy - kQBufs + 1; g <= last_copy; ++g)
+        if (g >= 0) mbar_wait_bounded(smem_u32(&ctl.ld_full[g % kQBufs]), (g / kQBufs) & 1, &zero, timeout_ns);
     }
   } else if (warp == 5) {
     // ================================================================ MMA issuer
@@ -319,63 +355,91 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr uint32_t idesc_s = make_idesc_f16(kT, kT, BF16 ? 1 : 0, 0);       // S^T, dP^T (M = keys)
       constexpr uint32_t idesc_kv = make_idesc_f16(kT, D, BF16 ? 1 : 0, 1);       // dV, dK (B M/N-major)
       constexpr uint32_t idesc_q = make_idesc_f16(kT, 64, BF16 ? 1 : 0, 1, 1);    // dQ half (A and B M/N-major)
-      const uint32_t sK = base + C::kOffK, sV = base + C::kOffV, sDS = base + C::kOffDS;
-      bool ok = mbar_wait_bounded(smem_u32(&ctl.kv_full), 0, abort_flag, timeout_ns);
-      uint32_t lt = 0;  // live query tiles done
-      for (int qi = 0; ok && qi < QT; ++qi) {
-        const int b = qi % kQBufs;
-        const uint32_t sQ = base + C::kOffQ + b * kTileBytes, sDO = base + C::kOffDO + b * kTileBytes;
-        // Tile qi's staging, and tile qi-1 finished (its TMEM results read).
-        if (!mbar_wait_bounded(smem_u32(&ctl.ld_full[b]), (qi / kQBufs) & 1, abort_flag, timeout_ns) ||
-            (qi > 0 && !mbar_wait_bounded(smem_u32(&ctl.tile_free[(qi - 1) % kQBufs]), ((qi - 1) / kQBufs) & 1,
-                                          abort_flag, timeout_ns))) {
+      const uint32_t sDS = base + C::kOffDS;
+      bool ok = true;
+      int gq = 0;
+      uint32_t lt = 0;
+      for (int j = 0; ok && j < n_items; ++j) {
+        const int bkv = j % kKVBufs;
+        const uint32_t sK = base + C::kOffK + bkv * kTileBytes, sV = base + C::kOffV + bkv * kTileBytes;
+        if (!mbar_wait_bounded(smem_u32(&ctl.kv_full[bkv]), (j / kKVBufs) & 1, abort_flag, timeout_ns)) {
           ok = false;
           break;
         }
-        if (ctl.live[b] != 0u) {
-          tc_fence_after();
-          // 16 head dims per step: swizzle chunk kk/4 of the rows, 32 bytes into it.
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * (kT * 128) + (kk & 3) * 32;
-            mma_ss(tmem + kColS, smem_desc_sw128(sK + off, 16, 1024), smem_desc_sw128(sQ + off, 16, 1024), idesc_s,
-                   kk > 0 ? 1u : 0u);
-          }
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * (kT * 128) + (kk & 3) * 32;
-            mma_ss(tmem + kColDP, smem_desc_sw128(sV + off, 16, 1024), smem_desc_sw128(sDO + off, 16, 1024), idesc_s,
-                   kk > 0 ? 1u : 0u);
-          }
-          mma_commit(smem_u32(&ctl.st_full));
-          if (!mbar_wait_bounded(smem_u32(&ctl.p_full), lt & 1, abort_flag, timeout_ns)) {
+        uint32_t item_lt = 0;  // live query tiles of this item so far
+        for (int qi = 0; qi < QT; ++qi, ++gq) {
+          const int b = gq % kQBufs;
+          const uint32_t sQ = base + C::kOffQ + b * kTileBytes, sDO = base + C::kOffDO + b * kTileBytes;
+          // Tile gq staged; when dQ_part shares TMEM columns with S^T / dP^T,
+          // also tile gq-1 finished (its dQ_part read).
+          if (!mbar_wait_bounded(smem_u32(&ctl.ld_full[b]), (gq / kQBufs) & 1, abort_flag, timeout_ns) ||
+              (!C::kDQApart && gq > 0 &&
+               !mbar_wait_bounded(smem_u32(&ctl.tile_free[(gq - 1) % kQBufs]), ((gq - 1) / kQBufs) & 1, abort_flag,
+                                  timeout_ns))) {
             ok = false;
             break;
           }
-          tc_fence_after();
-          // 16 query rows per step: 8 packed TMEM columns of P^T / dS^T, 2048
-          // bytes (16 rows of 128) into the M/N-major shared-memory operands,
-          // whose 64-dim chunks (D = 128) are kT * 128 bytes apart.
+          if (ctl.live[b] != 0u) {
+            // With dQ_part in its own columns, S^T / dP^T may be overwritten as
+            // soon as the previous live tile's products (which read P^T / dS^T
+            // from them) are complete; MMAs into different accumulators are not
+            // ordered by issue, so wait for that tile's commit.
+            if (C::kDQApart && lt > 0 &&
+                !mbar_wait_bounded(smem_u32(&ctl.dq_full), (lt - 1) & 1, abort_flag, timeout_ns)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            // 16 head dims per step: swizzle chunk kk/4 of the rows, 32 bytes into it.
 #pragma unroll
-          for (int kk = 0; kk < kT / 16; ++kk)
-            mma_ts(tmem + kColDV, tmem + kColS + kk * 8, smem_desc_sw128(sDO + kk * 2048, kT * 128, 1024),
-                   idesc_kv, (lt > 0 || kk > 0) ? 1u : 0u);
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t off = (kk >> 2) * (kT * 128) + (kk & 3) * 32;
+              mma_ss(tmem + kColS, smem_desc_sw128(sK + off, 16, 1024), smem_desc_sw128(sQ + off, 16, 1024),
+                     idesc_s, kk > 0 ? 1u : 0u);
+            }
 #pragma unroll
-          for (int kk = 0; kk < kT / 16; ++kk)
-            mma_ts(tmem + C::kColDK, tmem + kColDP + kk * 8, smem_desc_sw128(sQ + kk * 2048, kT * 128, 1024),
-                   idesc_kv, (lt > 0 || kk > 0) ? 1u : 0u);
-          // dQ_part = dS K in 64-dim halves: 16 keys per step; dS's two
-          // 64-query chunks are kT * 128 bytes apart, as are K's 64-dim chunks.
-#pragma unroll
-          for (int h = 0; h < C::kDChunks; ++h)
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t off = (kk >> 2) * (kT * 128) + (kk & 3) * 32;
+              mma_ss(tmem + kColDP, smem_desc_sw128(sV + off, 16, 1024), smem_desc_sw128(sDO + off, 16, 1024),
+                     idesc_s, kk > 0 ? 1u : 0u);
+            }
+            mma_commit(smem_u32(&ctl.st_full));
+            // P^T / dS^T of this tile; before the first dV / dK product of
+            // item j, the compute warps must have read item j-1's dV / dK.
+            if (!mbar_wait_bounded(smem_u32(&ctl.p_full), lt & 1, abort_flag, timeout_ns) ||
+                (item_lt == 0 && j > 0 &&
+                 !mbar_wait_bounded(smem_u32(&ctl.acc_free), (j - 1) & 1, abort_flag, timeout_ns))) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            // 16 query rows per step: 8 packed TMEM columns of P^T / dS^T, 2048
+            // bytes (16 rows of 128) into the M/N-major shared-memory operands,
+            // whose 64-dim chunks (D = 128) are kT * 128 bytes apart.
 #pragma unroll
             for (int kk = 0; kk < kT / 16; ++kk)
-              mma_ss(tmem + C::col_dq(h), smem_desc_sw128(sDS + kk * 2048, kT * 128, 1024),
-                     smem_desc_sw128(sK + h * (kT * 128) + kk * 2048, kT * 128, 1024), idesc_q, kk > 0 ? 1u : 0u);
-          mma_commit(smem_u32(&ctl.dq_full));
-          ++lt;
+              mma_ts(tmem + kColDV, tmem + kColS + kk * 8, smem_desc_sw128(sDO + kk * 2048, kT * 128, 1024),
+                     idesc_kv, (item_lt > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+            for (int kk = 0; kk < kT / 16; ++kk)
+              mma_ts(tmem + C::kColDK, tmem + kColDP + kk * 8, smem_desc_sw128(sQ + kk * 2048, kT * 128, 1024),
+                     idesc_kv, (item_lt > 0 || kk > 0) ? 1u : 0u);
+            // dQ_part = dS K in 64-dim halves: 16 keys per step; dS's two
+            // 64-query chunks are kT * 128 bytes apart, as are K's 64-dim chunks.
+#pragma unroll
+            for (int h = 0; h < C::kDChunks; ++h)
+#pragma unroll
+              for (int kk = 0; kk < kT / 16; ++kk)
+                mma_ss(tmem + C::col_dq(h), smem_desc_sw128(sDS + kk * 2048, kT * 128, 1024),
+                       smem_desc_sw128(sK + h * (kT * 128) + kk * 2048, kT * 128, 1024), idesc_q, kk > 0 ? 1u : 0u);
+            mma_commit(smem_u32(&ctl.dq_full));
+            ++lt;
+            ++item_lt;
+          }
+          mbar_arrive(smem_u32(&ctl.tile_free[b]));
         }
-        mbar_arrive(smem_u32(&ctl.tile_free[b]));
+        // K/V buffer bkv may be refilled once this item's MMAs are complete.
+        if (ok) mma_commit(smem_u32(&ctl.kv_free[bkv]));
       }
       if (!ok) fail();
       // Every MMA this thread issued must complete before TMEM is released.
@@ -391,6 +455,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int my_word = (t >> 5) * kT;  // the word holding this key, for each query row
     const int kb = t & 31;
     bool ok = true;
+    int gq = 0;
     uint32_t lt = 0;
     auto wait_all = [&](uint64_t& bar, uint32_t parity) -> bool {
       const bool all =
@@ -403,108 +468,119 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&bar));
     };
-    for (int qi = 0; qi < QT; ++qi) {
-      const int b = qi % kQBufs;
-      const uint32_t* my_words = s_mask + b * 4 * kT + my_word;
-      const float* t_lse = s_lse + b * kT;
-      const float* t_delta = s_delta + b * kT;
-      if (ok) ok = wait_all(ctl.ld_full[b], (qi / kQBufs) & 1);
-      if (ok && ctl.live[b] != 0u) {
-        ok = wait_all(ctl.st_full, lt & 1);
-        if (ok) {
-#pragma unroll 1
-          for (int c = 0; c < kT / 32; ++c) {
-            float s[32], dp[32];
-            tmem_ld32f(t_lane + kColS + c * 32, s);
-            tmem_ld32f(t_lane + kColDP + c * 32, dp);
-            tmem_wait_ld();
-            uint32_t pw[16], dw[16];
-#pragma unroll
-            for (int e = 0; e < 32; e += 4) {
-              const uint4 m4 = *reinterpret_cast<const uint4*>(my_words + c * 32 + e);
-              const float4 l4 = *reinterpret_cast<const float4*>(t_lse + c * 32 + e);
-              const float4 d4 = *reinterpret_cast<const float4*>(t_delta + c * 32 + e);
-              const uint32_t mm[4] = {m4.x, m4.y, m4.z, m4.w};
-              const float ll[4] = {l4.x, l4.y, l4.z, l4.w}, dd[4] = {d4.x, d4.y, d4.z, d4.w};
-              float p[4], ds[4];
-#pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                p[u] = ((mm[u] >> kb) & 1u) ? ex2f(fmaf(s[e + u], c2, -ll[u])) : 0.f;
-                ds[u] = p[u] * (dp[e + u] - dd[u]);
-              }
-              pw[e / 2] = pack2<BF16>(p[0], p[1]);
-              pw[e / 2 + 1] = pack2<BF16>(p[2], p[3]);
-              dw[e / 2] = pack2<BF16>(ds[0], ds[1]);
-              dw[e / 2 + 1] = pack2<BF16>(ds[2], ds[3]);
-            }
-            // P^T and dS^T over the S^T / dP^T columns already read (chunk c
-            // writes columns 16c.., whose values belong to chunks <= c).
-            tmem_st16(t_lane + kColS + c * 16, pw);
-            tmem_st16(t_lane + kColDP + c * 16, dw);
-            // dS for the dQ MMA: row t of the M-major operand, queries
-            // 32c .. 32c+31 = 16-byte chunks 4(c&1) .. +3 of 64-query chunk c/2,
-            // 128-byte swizzle (chunk index XOR row % 8).
-            uint8_t* drow = smem + C::kOffDS + (c >> 1) * (kT * 128) + t * 128;
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-              *reinterpret_cast<uint4*>(drow + ((((c & 1) * 4 + j) ^ (t & 7)) * 16)) =
-                  make_uint4(dw[4 * j], dw[4 * j + 1], dw[4 * j + 2], dw[4 * j + 3]);
-          }
-          tmem_wait_st();
-          fence_proxy_async_smem();  // dS written by this thread, read by the tensor core
-          arrive_warp(ctl.p_full);
-          ok = wait_all(ctl.dq_full, lt & 1);
+    for (int j = 0; ok && j < n_items; ++j) {
+      const int item = static_cast<int>(blockIdx.x) + j * G;
+      const int bh = item / KT;
+      const int key = (item - bh * KT) * kT + t;
+      uint32_t item_lt = 0;
+      for (int qi = 0; ok && qi < QT; ++qi, ++gq) {
+        const int b = gq % kQBufs;
+        const uint32_t* my_words = s_mask + b * 4 * kT + my_word;
+        const float* t_lse = s_lse + b * kT;
+        const float* t_delta = s_delta + b * kT;
+        ok = wait_all(ctl.ld_full[b], (gq / kQBufs) & 1);
+        if (ok && ctl.live[b] != 0u) {
+          ok = wait_all(ctl.st_full, lt & 1);
           if (ok) {
-            // dQ_part row t = query row qi*128 + t, scaled, added into the accumulator.
-            const int row = qi * kT + t;
 #pragma unroll 1
-            for (int h = 0; h < D / 32; ++h) {
-              uint32_t u[32];
-              tmem_ld32(t_lane + C::col_dq(h >> 1) + (h & 1) * 32, u);
+            for (int c = 0; c < kT / 32; ++c) {
+              float s[32], dp[32];
+              tmem_ld32f(t_lane + kColS + c * 32, s);
+              tmem_ld32f(t_lane + kColDP + c * 32, dp);
               tmem_wait_ld();
-              if (row < N) {
-                float* dst = dq_acc + (static_cast<int64_t>(bh) * N + row) * D + h * 32;
+              uint32_t pw[16], dw[16];
 #pragma unroll
-                for (int q4 = 0; q4 < 8; ++q4)
-                  red_add_v4(dst + 4 * q4, __uint_as_float(u[4 * q4]) * scale, __uint_as_float(u[4 * q4 + 1]) * scale,
-                             __uint_as_float(u[4 * q4 + 2]) * scale, __uint_as_float(u[4 * q4 + 3]) * scale);
+              for (int e = 0; e < 32; e += 4) {
+                const uint4 m4 = *reinterpret_cast<const uint4*>(my_words + c * 32 + e);
+                const float4 l4 = *reinterpret_cast<const float4*>(t_lse + c * 32 + e);
+                const float4 d4 = *reinterpret_cast<const float4*>(t_delta + c * 32 + e);
+                const uint32_t mm[4] = {m4.x, m4.y, m4.z, m4.w};
+                const float ll[4] = {l4.x, l4.y, l4.z, l4.w}, dd[4] = {d4.x, d4.y, d4.z, d4.w};
+                float p[4], ds[4];
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                  p[u] = ((mm[u] >> kb) & 1u) ? ex2f(fmaf(s[e + u], c2, -ll[u])) : 0.f;
+                  ds[u] = p[u] * (dp[e + u] - dd[u]);
+                }
+                pw[e / 2] = pack2<BF16>(p[0], p[1]);
+                pw[e / 2 + 1] = pack2<BF16>(p[2], p[3]);
+                dw[e / 2] = pack2<BF16>(ds[0], ds[1]);
+                dw[e / 2 + 1] = pack2<BF16>(ds[2], ds[3]);
+              }
+              // P^T and dS^T over the S^T / dP^T columns already read (chunk c
+              // writes columns 16c.., whose values belong to chunks <= c).
+              tmem_st16(t_lane + kColS + c * 16, pw);
+              tmem_st16(t_lane + kColDP + c * 16, dw);
+              // dS for the dQ MMA: row t of the M-major operand, queries
+              // 32c .. 32c+31 = 16-byte chunks 4(c&1) .. +3 of 64-query chunk c/2,
+              // 128-byte swizzle (chunk index XOR row % 8).
+              uint8_t* drow = smem + C::kOffDS + (c >> 1) * (kT * 128) + t * 128;
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                *reinterpret_cast<uint4*>(drow + ((((c & 1) * 4 + q) ^ (t & 7)) * 16)) =
+                    make_uint4(dw[4 * q], dw[4 * q + 1], dw[4 * q + 2], dw[4 * q + 3]);
+            }
+            tmem_wait_st();
+            fence_proxy_async_smem();  // dS written by this thread, read by the tensor core
+            arrive_warp(ctl.p_full);
+            ok = wait_all(ctl.dq_full, lt & 1);
+            if (ok) {
+              // dQ_part row t = query row qi*128 + t, scaled, added into the accumulator.
+              const int row = qi * kT + t;
+#pragma unroll 1
+              for (int h = 0; h < D / 32; ++h) {
+                uint32_t u[32];
+                tmem_ld32(t_lane + C::col_dq(h >> 1) + (h & 1) * 32, u);
+                tmem_wait_ld();
+                if (row < N) {
+                  float* dst = dq_acc + (static_cast<int64_t>(bh) * N + row) * D + h * 32;
+#pragma unroll
+                  for (int q4 = 0; q4 < 8; ++q4)
+                    red_add_v4(dst + 4 * q4, __uint_as_float(u[4 * q4]) * scale,
+                               __uint_as_float(u[4 * q4 + 1]) * scale, __uint_as_float(u[4 * q4 + 2]) * scale,
+                               __uint_as_float(u[4 * q4 + 3]) * scale);
+                }
               }
             }
+            ++lt;
+            ++item_lt;
           }
-          ++lt;
         }
+        if (ok) arrive_warp(ctl.tile_free[b]);
       }
-      arrive_warp(ctl.tile_free[b]);
-    }
-    // dV and dK of this key tile (lane t = key k0 + t); zero when no query tile was live.
-    const int key = k0 + t;
+      if (!ok) break;
+      // dV and dK of this key tile (lane t = key); zero when no query tile was
+      // live.  The dq_full wait of the item's last live tile covered all of
+      // its MMAs.
 #pragma unroll 1
-    for (int h = 0; h < D / 32; ++h) {
-      uint32_t vw[16], kw[16];
-      if (ok && lt > 0) {
-        uint32_t u[32];
-        tmem_ld32(t_lane + kColDV + h * 32, u);
-        tmem_wait_ld();
+      for (int h = 0; h < D / 32; ++h) {
+        uint32_t vw[16], kw[16];
+        if (item_lt > 0) {
+          uint32_t u[32];
+          tmem_ld32(t_lane + kColDV + h * 32, u);
+          tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 16; ++e) vw[e] = pack2<BF16>(__uint_as_float(u[2 * e]), __uint_as_float(u[2 * e + 1]));
-        tmem_ld32(t_lane + C::kColDK + h * 32, u);
-        tmem_wait_ld();
+          for (int e = 0; e < 16; ++e) vw[e] = pack2<BF16>(__uint_as_float(u[2 * e]), __uint_as_float(u[2 * e + 1]));
+          tmem_ld32(t_lane + C::kColDK + h * 32, u);
+          tmem_wait_ld();
 #pragma unroll
-        for (int e = 0; e < 16; ++e)
-          kw[e] = pack2<BF16>(__uint_as_float(u[2 * e]) * scale, __uint_as_float(u[2 * e + 1]) * scale);
-      } else {
+          for (int e = 0; e < 16; ++e)
+            kw[e] = pack2<BF16>(__uint_as_float(u[2 * e]) * scale, __uint_as_float(u[2 * e + 1]) * scale);
+        } else {
 #pragma unroll
-        for (int e = 0; e < 16; ++e) vw[e] = kw[e] = 0u;
-      }
-      if (key < N && ctl.abort_flag == 0) {
-        uint4* dvr = reinterpret_cast<uint4*>(dv + (static_cast<int64_t>(bh) * N + key) * D + h * 32);
-        uint4* dkr = reinterpret_cast<uint4*>(dk + (static_cast<int64_t>(bh) * N + key) * D + h * 32);
+          for (int e = 0; e < 16; ++e) vw[e] = kw[e] = 0u;
+        }
+        if (key < N) {
+          uint4* dvr = reinterpret_cast<uint4*>(dv + (static_cast<int64_t>(bh) * N + key) * D + h * 32);
+          uint4* dkr = reinterpret_cast<uint4*>(dk + (static_cast<int64_t>(bh) * N + key) * D + h * 32);
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          dvr[q] = make_uint4(vw[4 * q], vw[4 * q + 1], vw[4 * q + 2], vw[4 * q + 3]);
-          dkr[q] = make_uint4(kw[4 * q], kw[4 * q + 1], kw[4 * q + 2], kw[4 * q + 3]);
+          for (int q = 0; q < 4; ++q) {
+            dvr[q] = make_uint4(vw[4 * q], vw[4 * q + 1], vw[4 * q + 2], vw[4 * q + 3]);
+            dkr[q] = make_uint4(kw[4 * q], kw[4 * q + 1], kw[4 * q + 2], kw[4 * q + 3]);
+          }
         }
       }
+      arrive_warp(ctl.acc_free);
     }
     if (!ok && lane == 0) fail();
   }
@@ -541,7 +617,13 @@ int launch(const BwdParams& p, const char** msg) {
     return kErrCuda;
   }
   static bool smem_set[kMaxDevices] = {};
+  static int sms[kMaxDevices] = {};
   auto kern = attn_bwd_kernel<D, BF16>;
+  if (sms[dev] == 0 && cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    sms[dev] = 0;
+    *msg = "backward: cannot query the SM count";
+    return kErrCuda;
+  }
   if (!smem_set[dev]) {
     cudaError_t e =
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::kSmemBytes));
@@ -560,10 +642,13 @@ int launch(const BwdParams& p, const char** msg) {
   }
   if (e == cudaSuccess) {
     const int vec = (W % 4 == 0 && (reinterpret_cast<uintptr_t>(p.mask) & 15u) == 0) ? 1 : 0;
-    kern<<<static_cast<unsigned>(BH * KT), kThreads, C::kSmemBytes, p.stream>>>(
+    // One CTA per SM (168 KB of shared memory and all 512 TMEM columns each).
+    const int64_t items = BH * KT;
+    const int64_t grid = items < sms[dev] ? items : sms[dev];
+    kern<<<static_cast<unsigned>(grid), kThreads, C::kSmemBytes, p.stream>>>(
         mq, mk, mv, mdo, p.mask, p.lse, p.delta, p.dq_accum, static_cast<uint16_t*>(p.dk),
         static_cast<uint16_t*>(p.dv), static_cast<int>(N), static_cast<int>(W), static_cast<int>(KT),
-        static_cast<int>(QT), vec, p.scale, p.err_word, p.timeout_ns);
+        static_cast<int>(QT), static_cast<int>(items), vec, p.scale, p.err_word, p.timeout_ns);
     e = cudaGetLastError();
   }
   if (e == cudaSuccess) {
