@@ -26,10 +26,12 @@
 //                        global memory (red.global.add.v4.f32)
 //   bwd_dq_convert_kernel  FP32 accumulator -> dq in the input dtype
 //
-// Warps (192 threads): 0-3 compute (thread t <-> TMEM lane t), 4 loader
-// (TMA of K, V, Q, dO; mask words, LSE and Delta of the query tile staged in
-// shared memory), 5 MMA issuer and TMEM owner.  TMEM layout per head dim:
-// see BwdCfg.
+// Warps (320 threads): 0-3 compute (thread t <-> TMEM lane t; P^T and dS^T),
+// 4 loader (TMA of K, V, Q, dO; mask words, LSE and Delta of the query tile
+// staged in shared memory), 5 MMA issuer and TMEM owner, 6-9 epilogue (dQ_part
+// of each live tile into the FP32 accumulator, dK and dV of each item; warp w
+// reads TMEM lanes 32(w%4)..+31), so the epilogues of one tile overlap the
+// element-wise work of the next.  TMEM layout per head dim: see BwdCfg.
 // Every wait is bounded and reports through the device error word.
 #include <cfloat>
 #include <cuda_bf16.h>
@@ -42,7 +44,7 @@ namespace sma {
 namespace {
 
 constexpr int kT = 128;  // query rows and keys per tile
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
 constexpr int kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256;
 constexpr float kLog2e = 1.44269504088896340736f;
@@ -65,7 +67,7 @@ struct BwdCfg {
   static constexpr int kQBufs = D == 64 ? 2 : 1;
   static constexpr uint32_t kColDK = kColDV + D;
   __host__ __device__ static constexpr uint32_t col_dq(int h) { return D == 64 ? 384u : (h == 0 ? 64u : 192u); }
-  // The next tile's S^T / dP^T may be issued while the compute warps still
+  // The next tile's S^T / dP^T may be issued while the epilogue warps still
   // read this tile's dQ_part only when the two do not share TMEM columns.
   static constexpr bool kDQApart = D == 64;
   static constexpr int kOffK = 0;
@@ -85,12 +87,14 @@ struct BwdCfg {
 struct BwdCtl {
   uint64_t kv_full[2];    // K and V of an item landed in buffer b
   uint64_t kv_free[2];    // MMAs of the item in K/V buffer b complete (committed by the MMA issuer)
-  uint64_t acc_free;      // dV and dK of an item read out of TMEM (4 compute warps)
+  uint64_t acc_free;      // dV and dK of an item read out of TMEM (4 epilogue warps)
   uint64_t ld_full[2];    // query tile staged in buffer b (Q, dO by TMA; mask, LSE, Delta by the loader warp)
   uint64_t st_full;       // S^T and dP^T complete
   uint64_t p_full;        // P^T, dS^T in TMEM and dS in shared memory (4 compute warps)
-  uint64_t dq_full;       // dV, dK, dQ_part MMAs complete
-  uint64_t tile_free[2];  // compute warps and MMA issuer done with buffer b (5 arrivals)
+  uint64_t pt_free;       // dV, dK products of a tile complete (they read P^T / dS^T in TMEM)
+  uint64_t dq_full;       // all products of a tile complete (dQ_part in TMEM)
+  uint64_t dq_free;       // dQ_part of a tile read out of TMEM (4 epilogue warps)
+  uint64_t tile_free[2];  // compute, epilogue warps and the MMA issuer done with buffer b (9 arrivals)
   uint64_t drain;
   uint32_t tmem_base;
   uint32_t live[2];
@@ -213,13 +217,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(smem_u32(&ctl.kv_full[b]), 1);
       mbar_init(smem_u32(&ctl.kv_free[b]), 1);
       mbar_init(smem_u32(&ctl.ld_full[b]), 1);
-      mbar_init(smem_u32(&ctl.tile_free[b]), 5);  // 4 compute warps + the MMA issuer
+      mbar_init(smem_u32(&ctl.tile_free[b]), 9);  // 4 compute + 4 epilogue warps + the MMA issuer
       ctl.live[b] = 0;
     }
     mbar_init(smem_u32(&ctl.acc_free), 4);
     mbar_init(smem_u32(&ctl.st_full), 1);
     mbar_init(smem_u32(&ctl.p_full), 4);
+    mbar_init(smem_u32(&ctl.pt_free), 1);
     mbar_init(smem_u32(&ctl.dq_full), 1);
+    mbar_init(smem_u32(&ctl.dq_free), 4);
     mbar_init(smem_u32(&ctl.drain), 1);
     ctl.abort_flag = 0;
     fence_barrier_init();
@@ -277,8 +283,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++kv_copies;
       for (int qi = 0; qi < QT; ++qi, ++gq) {
         const int b = gq % kQBufs;
-        // Buffer b is free once the compute warps and the MMA issuer are done
-        // with tile gq - kQBufs (its MMAs have completed by then).
+        // Buffer b is free once the compute and epilogue warps are done with
+        // tile gq - kQBufs and the products reading its Q / dO are complete
+        // (the MMA issuer's arrival is a tcgen05.commit for a live tile).
         if (gq >= kQBufs &&
             !__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&ctl.tile_free[b]), ((gq - kQBufs) / kQBufs) & 1,
                                                        abort_flag, timeout_ns))) {
@@ -286,39 +293,44 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         const int i0 = qi * kT;
+        // All global loads of the tile (4 rows per lane) are issued before any
+        // of them is used, so their latencies overlap.
+        uint32_t w4[4][4];
+        float l2[4], de[4];
+#pragma unroll
+        for (int rr = 0; rr < 4; ++rr) {
+          const int row = i0 + lane + 32 * rr;
+          const bool in = row < N;
+          const int64_t r64 = static_cast<int64_t>(bh) * N + (in ? row : 0);
+          const uint32_t* mrow = mask + r64 * W + kt * 4;
+          if (vec) {
+            uint4 x = make_uint4(0u, 0u, 0u, 0u);
+            if (in) x = __ldg(reinterpret_cast<const uint4*>(mrow));
+            w4[rr][0] = x.x;
+            w4[rr][1] = x.y;
+            w4[rr][2] = x.z;
+            w4[rr][3] = x.w;
+          } else {
+#pragma unroll
+            for (int w = 0; w < 4; ++w) w4[rr][w] = (in && kt * 4 + w < W) ? __ldg(mrow + w) : 0u;
+          }
+          l2[rr] = in ? __ldg(lse + r64) : 0.f;
+          de[rr] = in ? __ldg(delta + r64) : 0.f;
+        }
         uint32_t any = 0u;
 #pragma unroll
         for (int rr = 0; rr < 4; ++rr) {
           const int i = lane + 32 * rr;
-          const int row = i0 + i;
-          uint32_t w4[4] = {0u, 0u, 0u, 0u};
-          float l2 = 0.f, de = 0.f;
-          if (row < N) {
-            const uint32_t* mrow = mask + (static_cast<int64_t>(bh) * N + row) * W + kt * 4;
-            if (vec) {
-              const uint4 x = __ldg(reinterpret_cast<const uint4*>(mrow));
-              w4[0] = x.x;
-              w4[1] = x.y;
-              w4[2] = x.z;
-              w4[3] = x.w;
-            } else {
-#pragma unroll
-              for (int w = 0; w < 4; ++w) w4[w] = (kt * 4 + w < W) ? __ldg(mrow + w) : 0u;
-            }
-#pragma unroll
-            for (int w = 0; w < 4; ++w) w4[w] &= valid_bits(kt * 4 + w, N);
-            // -FLT_MAX (a row with no kept key) becomes -inf; such a row has no
-            // mask bit, so its P is 0 by the select and never uses this value.
-            l2 = lse[static_cast<int64_t>(bh) * N + row] * kLog2e;
-            de = delta[static_cast<int64_t>(bh) * N + row];
-          }
 #pragma unroll
           for (int w = 0; w < 4; ++w) {
-            s_mask[b * 4 * kT + w * kT + i] = w4[w];
-            any |= w4[w];
+            const uint32_t x = w4[rr][w] & valid_bits(kt * 4 + w, N);
+            s_mask[b * 4 * kT + w * kT + i] = x;
+            any |= x;
           }
-          s_lse[b * kT + i] = l2;
-          s_delta[b * kT + i] = de;
+          // -FLT_MAX (a row with no kept key) becomes -inf; such a row has no
+          // mask bit, so its P is 0 by the select and never uses this value.
+          s_lse[b * kT + i] = l2[rr] * kLog2e;
+          s_delta[b * kT + i] = de[rr];
         }
         const bool live = __any_sync(0xffffffffu, any != 0u);
         __syncwarp();
@@ -370,73 +382,82 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int qi = 0; qi < QT; ++qi, ++gq) {
           const int b = gq % kQBufs;
           const uint32_t sQ = base + C::kOffQ + b * kTileBytes, sDO = base + C::kOffDO + b * kTileBytes;
-          // Tile gq staged; when dQ_part shares TMEM columns with S^T / dP^T,
-          // also tile gq-1 finished (its dQ_part read).
-          if (!mbar_wait_bounded(smem_u32(&ctl.ld_full[b]), (gq / kQBufs) & 1, abort_flag, timeout_ns) ||
-              (!C::kDQApart && gq > 0 &&
-               !mbar_wait_bounded(smem_u32(&ctl.tile_free[(gq - 1) % kQBufs]), ((gq - 1) / kQBufs) & 1, abort_flag,
-                                  timeout_ns))) {
+          if (!mbar_wait_bounded(smem_u32(&ctl.ld_full[b]), (gq / kQBufs) & 1, abort_flag, timeout_ns)) {
             ok = false;
             break;
           }
-          if (ctl.live[b] != 0u) {
-            // With dQ_part in its own columns, S^T / dP^T may be overwritten as
-            // soon as the previous live tile's products (which read P^T / dS^T
-            // from them) are complete; MMAs into different accumulators are not
-            // ordered by issue, so wait for that tile's commit.
-            if (C::kDQApart && lt > 0 &&
-                !mbar_wait_bounded(smem_u32(&ctl.dq_full), (lt - 1) & 1, abort_flag, timeout_ns)) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            // 16 head dims per step: swizzle chunk kk/4 of the rows, 32 bytes into it.
-#pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk) {
-              const uint32_t off = (kk >> 2) * (kT * 128) + (kk & 3) * 32;
-              mma_ss(tmem + kColS, smem_desc_sw128(sK + off, 16, 1024), smem_desc_sw128(sQ + off, 16, 1024),
-                     idesc_s, kk > 0 ? 1u : 0u);
-            }
-#pragma unroll
-            for (int kk = 0; kk < D / 16; ++kk) {
-              const uint32_t off = (kk >> 2) * (kT * 128) + (kk & 3) * 32;
-              mma_ss(tmem + kColDP, smem_desc_sw128(sV + off, 16, 1024), smem_desc_sw128(sDO + off, 16, 1024),
-                     idesc_s, kk > 0 ? 1u : 0u);
-            }
-            mma_commit(smem_u32(&ctl.st_full));
-            // P^T / dS^T of this tile; before the first dV / dK product of
-            // item j, the compute warps must have read item j-1's dV / dK.
-            if (!mbar_wait_bounded(smem_u32(&ctl.p_full), lt & 1, abort_flag, timeout_ns) ||
-                (item_lt == 0 && j > 0 &&
-                 !mbar_wait_bounded(smem_u32(&ctl.acc_free), (j - 1) & 1, abort_flag, timeout_ns))) {
-              ok = false;
-              break;
-            }
-            tc_fence_after();
-            // 16 query rows per step: 8 packed TMEM columns of P^T / dS^T, 2048
-            // bytes (16 rows of 128) into the M/N-major shared-memory operands,
-            // whose 64-dim chunks (D = 128) are kT * 128 bytes apart.
-#pragma unroll
-            for (int kk = 0; kk < kT / 16; ++kk)
-              mma_ts(tmem + kColDV, tmem + kColS + kk * 8, smem_desc_sw128(sDO + kk * 2048, kT * 128, 1024),
-                     idesc_kv, (item_lt > 0 || kk > 0) ? 1u : 0u);
-#pragma unroll
-            for (int kk = 0; kk < kT / 16; ++kk)
-              mma_ts(tmem + C::kColDK, tmem + kColDP + kk * 8, smem_desc_sw128(sQ + kk * 2048, kT * 128, 1024),
-                     idesc_kv, (item_lt > 0 || kk > 0) ? 1u : 0u);
-            // dQ_part = dS K in 64-dim halves: 16 keys per step; dS's two
-            // 64-query chunks are kT * 128 bytes apart, as are K's 64-dim chunks.
-#pragma unroll
-            for (int h = 0; h < C::kDChunks; ++h)
-#pragma unroll
-              for (int kk = 0; kk < kT / 16; ++kk)
-                mma_ss(tmem + C::col_dq(h), smem_desc_sw128(sDS + kk * 2048, kT * 128, 1024),
-                       smem_desc_sw128(sK + h * (kT * 128) + kk * 2048, kT * 128, 1024), idesc_q, kk > 0 ? 1u : 0u);
-            mma_commit(smem_u32(&ctl.dq_full));
-            ++lt;
-            ++item_lt;
+          if (ctl.live[b] == 0u) {
+            mbar_arrive(smem_u32(&ctl.tile_free[b]));
+            continue;
           }
-          mbar_arrive(smem_u32(&ctl.tile_free[b]));
+          // The S^T / dP^T columns are free once the previous live tile's dV /
+          // dK products (which read P^T / dS^T there) are complete and, where
+          // dQ_part shares those columns (D = 128), its dQ_part has been read.
+          // MMAs into different accumulators are not ordered by issue.
+          if (lt > 0 && !mbar_wait_bounded(smem_u32(C::kDQApart ? &ctl.pt_free : &ctl.dq_free), (lt - 1) & 1,
+                                           abort_flag, timeout_ns)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // 16 head dims per step: swizzle chunk kk/4 of the rows, 32 bytes into it.
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * (kT * 128) + (kk & 3) * 32;
+            mma_ss(tmem + kColS, smem_desc_sw128(sK + off, 16, 1024), smem_desc_sw128(sQ + off, 16, 1024), idesc_s,
+                   kk > 0 ? 1u : 0u);
+          }
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const uint32_t off = (kk >> 2) * (kT * 128) + (kk & 3) * 32;
+            mma_ss(tmem + kColDP, smem_desc_sw128(sV + off, 16, 1024), smem_desc_sw128(sDO + off, 16, 1024), idesc_s,
+                   kk > 0 ? 1u : 0u);
+          }
+          // st_full also covers every earlier product, so dQ_part of the
+          // previous tile has read dS from shared memory before it is rewritten.
+          mma_commit(smem_u32(&ctl.st_full));
+          // P^T / dS^T of this tile; before the first dV / dK product of item
+          // j, the epilogue warps must have read item j-1's dV / dK.
+          if (!mbar_wait_bounded(smem_u32(&ctl.p_full), lt & 1, abort_flag, timeout_ns) ||
+              (item_lt == 0 && j > 0 &&
+               !mbar_wait_bounded(smem_u32(&ctl.acc_free), (j - 1) & 1, abort_flag, timeout_ns))) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // 16 query rows per step: 8 packed TMEM columns of P^T / dS^T, 2048
+          // bytes (16 rows of 128) into the M/N-major shared-memory operands,
+          // whose 64-dim chunks (D = 128) are kT * 128 bytes apart.
+#pragma unroll
+          for (int kk = 0; kk < kT / 16; ++kk)
+            mma_ts(tmem + kColDV, tmem + kColS + kk * 8, smem_desc_sw128(sDO + kk * 2048, kT * 128, 1024), idesc_kv,
+                   (item_lt > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+          for (int kk = 0; kk < kT / 16; ++kk)
+            mma_ts(tmem + C::kColDK, tmem + kColDP + kk * 8, smem_desc_sw128(sQ + kk * 2048, kT * 128, 1024),
+                   idesc_kv, (item_lt > 0 || kk > 0) ? 1u : 0u);
+          if constexpr (C::kDQApart) {
+            mma_commit(smem_u32(&ctl.pt_free));
+            // dQ_part in its own columns: the previous tile's must have been read.
+            if (lt > 0 && !mbar_wait_bounded(smem_u32(&ctl.dq_free), (lt - 1) & 1, abort_flag, timeout_ns)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+          }
+          // dQ_part = dS K in 64-dim halves: 16 keys per step; dS's two
+          // 64-query chunks are kT * 128 bytes apart, as are K's 64-dim chunks.
+#pragma unroll
+          for (int h = 0; h < C::kDChunks; ++h)
+#pragma unroll
+            for (int kk = 0; kk < kT / 16; ++kk)
+              mma_ss(tmem + C::col_dq(h), smem_desc_sw128(sDS + kk * 2048, kT * 128, 1024),
+                     smem_desc_sw128(sK + h * (kT * 128) + kk * 2048, kT * 128, 1024), idesc_q, kk > 0 ? 1u : 0u);
+          mma_commit(smem_u32(&ctl.dq_full));
+          // The staging buffer's Q / dO are released when these products complete.
+          mma_commit(smem_u32(&ctl.tile_free[b]));
+          ++lt;
+          ++item_lt;
         }
         // K/V buffer bkv may be refilled once this item's MMAs are complete.
         if (ok) mma_commit(smem_u32(&ctl.kv_free[bkv]));
@@ -448,15 +469,6 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_wait_bounded(smem_u32(&ctl.drain), 0, &zero, timeout_ns);
     }
   } else {
-    // ================================================================ compute
-    const int t = threadIdx.x;  // key row of the tile for P^T / dS^T / dK / dV, query row for dQ_part
-    const uint32_t t_lane = tmem + (static_cast<uint32_t>(warp * 32) << 16);
-    const float c2 = scale * kLog2e;
-    const int my_word = (t >> 5) * kT;  // the word holding this key, for each query row
-    const int kb = t & 31;
-    bool ok = true;
-    int gq = 0;
-    uint32_t lt = 0;
     auto wait_all = [&](uint64_t& bar, uint32_t parity) -> bool {
       const bool all =
           __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&bar), parity, abort_flag, timeout_ns));
@@ -468,119 +480,141 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&bar));
     };
-    for (int j = 0; ok && j < n_items; ++j) {
-      const int item = static_cast<int>(blockIdx.x) + j * G;
-      const int bh = item / KT;
-      const int key = (item - bh * KT) * kT + t;
-      uint32_t item_lt = 0;
-      for (int qi = 0; ok && qi < QT; ++qi, ++gq) {
+    // Warp w reads TMEM lanes 32(w%4)..+31: thread t is key t of the tile
+    // (P^T, dS^T, dK, dV) and query row t (dQ_part).
+    const int t = (warp & 3) * 32 + lane;
+    const uint32_t t_lane = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
+    bool ok = true;
+    int gq = 0;
+    uint32_t lt = 0;
+    if (warp < 4) {
+      // ============================================================== compute
+      const float c2 = scale * kLog2e;
+      const int my_word = (t >> 5) * kT;  // the word holding this key, for each query row
+      const int kb = t & 31;
+      const int n_tiles = n_items * QT;
+      for (; gq < n_tiles; ++gq) {
         const int b = gq % kQBufs;
         const uint32_t* my_words = s_mask + b * 4 * kT + my_word;
         const float* t_lse = s_lse + b * kT;
         const float* t_delta = s_delta + b * kT;
         ok = wait_all(ctl.ld_full[b], (gq / kQBufs) & 1);
-        if (ok && ctl.live[b] != 0u) {
+        if (!ok) break;
+        if (ctl.live[b] != 0u) {
           ok = wait_all(ctl.st_full, lt & 1);
-          if (ok) {
+          if (!ok) break;
 #pragma unroll 1
-            for (int c = 0; c < kT / 32; ++c) {
-              float s[32], dp[32];
-              tmem_ld32f(t_lane + kColS + c * 32, s);
-              tmem_ld32f(t_lane + kColDP + c * 32, dp);
-              tmem_wait_ld();
-              uint32_t pw[16], dw[16];
+          for (int c = 0; c < kT / 32; ++c) {
+            float s[32], dp[32];
+            tmem_ld32f(t_lane + kColS + c * 32, s);
+            tmem_ld32f(t_lane + kColDP + c * 32, dp);
+            tmem_wait_ld();
+            uint32_t pw[16], dw[16];
 #pragma unroll
-              for (int e = 0; e < 32; e += 4) {
-                const uint4 m4 = *reinterpret_cast<const uint4*>(my_words + c * 32 + e);
-                const float4 l4 = *reinterpret_cast<const float4*>(t_lse + c * 32 + e);
-                const float4 d4 = *reinterpret_cast<const float4*>(t_delta + c * 32 + e);
-                const uint32_t mm[4] = {m4.x, m4.y, m4.z, m4.w};
-                const float ll[4] = {l4.x, l4.y, l4.z, l4.w}, dd[4] = {d4.x, d4.y, d4.z, d4.w};
-                float p[4], ds[4];
+            for (int e = 0; e < 32; e += 4) {
+              const uint4 m4 = *reinterpret_cast<const uint4*>(my_words + c * 32 + e);
+              const float4 l4 = *reinterpret_cast<const float4*>(t_lse + c * 32 + e);
+              const float4 d4 = *reinterpret_cast<const float4*>(t_delta + c * 32 + e);
+              const uint32_t mm[4] = {m4.x, m4.y, m4.z, m4.w};
+              const float ll[4] = {l4.x, l4.y, l4.z, l4.w}, dd[4] = {d4.x, d4.y, d4.z, d4.w};
+              float p[4], ds[4];
 #pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                  p[u] = ((mm[u] >> kb) & 1u) ? ex2f(fmaf(s[e + u], c2, -ll[u])) : 0.f;
-                  ds[u] = p[u] * (dp[e + u] - dd[u]);
-                }
-                pw[e / 2] = pack2<BF16>(p[0], p[1]);
-                pw[e / 2 + 1] = pack2<BF16>(p[2], p[3]);
-                dw[e / 2] = pack2<BF16>(ds[0], ds[1]);
-                dw[e / 2 + 1] = pack2<BF16>(ds[2], ds[3]);
+              for (int u = 0; u < 4; ++u) {
+                p[u] = ((mm[u] >> kb) & 1u) ? ex2f(fmaf(s[e + u], c2, -ll[u])) : 0.f;
+                ds[u] = p[u] * (dp[e + u] - dd[u]);
               }
-              // P^T and dS^T over the S^T / dP^T columns already read (chunk c
-              // writes columns 16c.., whose values belong to chunks <= c).
-              tmem_st16(t_lane + kColS + c * 16, pw);
-              tmem_st16(t_lane + kColDP + c * 16, dw);
-              // dS for the dQ MMA: row t of the M-major operand, queries
-              // 32c .. 32c+31 = 16-byte chunks 4(c&1) .. +3 of 64-query chunk c/2,
-              // 128-byte swizzle (chunk index XOR row % 8).
-              uint8_t* drow = smem + C::kOffDS + (c >> 1) * (kT * 128) + t * 128;
-#pragma unroll
-              for (int q = 0; q < 4; ++q)
-                *reinterpret_cast<uint4*>(drow + ((((c & 1) * 4 + q) ^ (t & 7)) * 16)) =
-                    make_uint4(dw[4 * q], dw[4 * q + 1], dw[4 * q + 2], dw[4 * q + 3]);
+              pw[e / 2] = pack2<BF16>(p[0], p[1]);
+              pw[e / 2 + 1] = pack2<BF16>(p[2], p[3]);
+              dw[e / 2] = pack2<BF16>(ds[0], ds[1]);
+              dw[e / 2 + 1] = pack2<BF16>(ds[2], ds[3]);
             }
-            tmem_wait_st();
-            fence_proxy_async_smem();  // dS written by this thread, read by the tensor core
-            arrive_warp(ctl.p_full);
-            ok = wait_all(ctl.dq_full, lt & 1);
-            if (ok) {
-              // dQ_part row t = query row qi*128 + t, scaled, added into the accumulator.
-              const int row = qi * kT + t;
+            // P^T and dS^T over the S^T / dP^T columns already read (chunk c
+            // writes columns 16c.., whose values belong to chunks <= c).
+            tmem_st16(t_lane + kColS + c * 16, pw);
+            tmem_st16(t_lane + kColDP + c * 16, dw);
+            // dS for the dQ MMA: row t of the M-major operand, queries
+            // 32c .. 32c+31 = 16-byte chunks 4(c&1) .. +3 of 64-query chunk c/2,
+            // 128-byte swizzle (chunk index XOR row % 8).
+            uint8_t* drow = smem + C::kOffDS + (c >> 1) * (kT * 128) + t * 128;
+#pragma unroll
+            for (int q = 0; q < 4; ++q)
+              *reinterpret_cast<uint4*>(drow + ((((c & 1) * 4 + q) ^ (t & 7)) * 16)) =
+                  make_uint4(dw[4 * q], dw[4 * q + 1], dw[4 * q + 2], dw[4 * q + 3]);
+          }
+          tmem_wait_st();
+          fence_proxy_async_smem();  // dS written by this thread, read by the tensor core
+          arrive_warp(ctl.p_full);
+          ++lt;
+        }
+        arrive_warp(ctl.tile_free[b]);
+      }
+    } else {
+      // ============================================================== epilogue
+      for (int j = 0; ok && j < n_items; ++j) {
+        const int item = static_cast<int>(blockIdx.x) + j * G;
+        const int bh = item / KT;
+        const int key = (item - bh * KT) * kT + t;
+        uint32_t item_lt = 0;
+        for (int qi = 0; qi < QT; ++qi, ++gq) {
+          const int b = gq % kQBufs;
+          ok = wait_all(ctl.ld_full[b], (gq / kQBufs) & 1);
+          if (!ok) break;
+          const bool live = ctl.live[b] != 0u;
+          arrive_warp(ctl.tile_free[b]);  // only live[b] is read from the buffer
+          if (!live) continue;
+          ok = wait_all(ctl.dq_full, lt & 1);
+          if (!ok) break;
+          // dQ_part row t = query row qi*128 + t: all of it into registers,
+          // TMEM released, then scaled and added into the accumulator.
+          float u[D];
+#pragma unroll
+          for (int h = 0; h < D / 32; ++h) tmem_ld32f(t_lane + C::col_dq(h >> 1) + (h & 1) * 32, u + 32 * h);
+          tmem_wait_ld();
+          arrive_warp(ctl.dq_free);
+          const int row = qi * kT + t;
+          if (row < N) {
+            float* dst = dq_acc + (static_cast<int64_t>(bh) * N + row) * D;
+#pragma unroll
+            for (int q4 = 0; q4 < D / 4; ++q4)
+              red_add_v4(dst + 4 * q4, u[4 * q4] * scale, u[4 * q4 + 1] * scale, u[4 * q4 + 2] * scale,
+                         u[4 * q4 + 3] * scale);
+          }
+          ++lt;
+          ++item_lt;
+        }
+        if (!ok) break;
+        // dV and dK of this key tile (lane t = key); zero when no query tile
+        // was live.  The dq_full wait of the item's last live tile covered all
+        // of its products.
 #pragma unroll 1
-              for (int h = 0; h < D / 32; ++h) {
-                uint32_t u[32];
-                tmem_ld32(t_lane + C::col_dq(h >> 1) + (h & 1) * 32, u);
-                tmem_wait_ld();
-                if (row < N) {
-                  float* dst = dq_acc + (static_cast<int64_t>(bh) * N + row) * D + h * 32;
+        for (int h = 0; h < D / 32; ++h) {
+          uint32_t vw[16], kw[16];
+          if (item_lt > 0) {
+            float u[32];
+            tmem_ld32f(t_lane + kColDV + h * 32, u);
+            tmem_wait_ld();
 #pragma unroll
-                  for (int q4 = 0; q4 < 8; ++q4)
-                    red_add_v4(dst + 4 * q4, __uint_as_float(u[4 * q4]) * scale,
-                               __uint_as_float(u[4 * q4 + 1]) * scale, __uint_as_float(u[4 * q4 + 2]) * scale,
-                               __uint_as_float(u[4 * q4 + 3]) * scale);
-                }
-              }
+            for (int e = 0; e < 16; ++e) vw[e] = pack2<BF16>(u[2 * e], u[2 * e + 1]);
+            tmem_ld32f(t_lane + C::kColDK + h * 32, u);
+            tmem_wait_ld();
+#pragma unroll
+            for (int e = 0; e < 16; ++e) kw[e] = pack2<BF16>(u[2 * e] * scale, u[2 * e + 1] * scale);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 16; ++e) vw[e] = kw[e] = 0u;
+          }
+          if (key < N) {
+            uint4* dvr = reinterpret_cast<uint4*>(dv + (static_cast<int64_t>(bh) * N + key) * D + h * 32);
+            uint4* dkr = reinterpret_cast<uint4*>(dk + (static_cast<int64_t>(bh) * N + key) * D + h * 32);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              dvr[q] = make_uint4(vw[4 * q], vw[4 * q + 1], vw[4 * q + 2], vw[4 * q + 3]);
+              dkr[q] = make_uint4(kw[4 * q], kw[4 * q + 1], kw[4 * q + 2], kw[4 * q + 3]);
             }
-            ++lt;
-            ++item_lt;
           }
         }
-        if (ok) arrive_warp(ctl.tile_free[b]);
+        arrive_warp(ctl.acc_free);
       }
-      if (!ok) break;
-      // dV and dK of this key tile (lane t = key); zero when no query tile was
-      // live.  The dq_full wait of the item's last live tile covered all of
-      // its MMAs.
-#pragma unroll 1
-      for (int h = 0; h < D / 32; ++h) {
-        uint32_t vw[16], kw[16];
-        if (item_lt > 0) {
-          uint32_t u[32];
-          tmem_ld32(t_lane + kColDV + h * 32, u);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 16; ++e) vw[e] = pack2<BF16>(__uint_as_float(u[2 * e]), __uint_as_float(u[2 * e + 1]));
-          tmem_ld32(t_lane + C::kColDK + h * 32, u);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 16; ++e)
-            kw[e] = pack2<BF16>(__uint_as_float(u[2 * e]) * scale, __uint_as_float(u[2 * e + 1]) * scale);
-        } else {
-#pragma unroll
-          for (int e = 0; e < 16; ++e) vw[e] = kw[e] = 0u;
-        }
-        if (key < N) {
-          uint4* dvr = reinterpret_cast<uint4*>(dv + (static_cast<int64_t>(bh) * N + key) * D + h * 32);
-          uint4* dkr = reinterpret_cast<uint4*>(dk + (static_cast<int64_t>(bh) * N + key) * D + h * 32);
-#pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            dvr[q] = make_uint4(vw[4 * q], vw[4 * q + 1], vw[4 * q + 2], vw[4 * q + 3]);
-            dkr[q] = make_uint4(kw[4 * q], kw[4 * q + 1], kw[4 * q + 2], kw[4 * q + 3]);
-          }
-        }
-      }
-      arrive_warp(ctl.acc_free);
     }
     if (!ok && lane == 0) fail();
   }
