@@ -258,6 +258,41 @@ __global__ void __launch_bounds__(kThreads, 1)
     int gq = 0;
     int last_copy = -1;  // last query tile (in gq) whose Q/dO copies were started
     int kv_copies = 0;   // items whose K/V copies were started
+    const int n_tiles = n_items * QT;
+    // Mask words, LSE and Delta of query tile g (4 rows per lane): all loads
+    // issued at once, into registers.
+    auto fetch = [&](int g, uint32_t (&w4)[4][4], float (&l2)[4], float (&de)[4]) {
+      const int jj = g / QT;
+      const int item = static_cast<int>(blockIdx.x) + jj * G;
+      const int fbh = item / KT;
+      const int fkt = item - fbh * KT;
+      const int i0 = (g - jj * QT) * kT;
+#pragma unroll
+      for (int rr = 0; rr < 4; ++rr) {
+        const int row = i0 + lane + 32 * rr;
+        const bool in = row < N;
+        const int64_t r64 = static_cast<int64_t>(fbh) * N + (in ? row : 0);
+        const uint32_t* mrow = mask + r64 * W + fkt * 4;
+        if (vec) {
+          uint4 x = make_uint4(0u, 0u, 0u, 0u);
+          if (in) x = __ldg(reinterpret_cast<const uint4*>(mrow));
+          w4[rr][0] = x.x;
+          w4[rr][1] = x.y;
+          w4[rr][2] = x.z;
+          w4[rr][3] = x.w;
+        } else {
+#pragma unroll
+          for (int w = 0; w < 4; ++w) w4[rr][w] = (in && fkt * 4 + w < W) ? __ldg(mrow + w) : 0u;
+        }
+        l2[rr] = in ? __ldg(lse + r64) : 0.f;
+        de[rr] = in ? __ldg(delta + r64) : 0.f;
+      }
+    };
+    // The loads of tile g+1 are issued before tile g waits for its buffer, so
+    // their latency overlaps a whole tile instead of delaying the staging.
+    uint32_t nw[4][4];
+    float nl[4], nd[4];
+    fetch(0, nw, nl, nd);
     for (int j = 0; ok && j < n_items; ++j) {
       const int item = static_cast<int>(blockIdx.x) + j * G;
       const int bh = item / KT;
@@ -283,6 +318,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       ++kv_copies;
       for (int qi = 0; qi < QT; ++qi, ++gq) {
         const int b = gq % kQBufs;
+        uint32_t w4[4][4];
+        float l2[4], de[4];
+#pragma unroll
+        for (int rr = 0; rr < 4; ++rr) {
+          l2[rr] = nl[rr];
+          de[rr] = nd[rr];
+#pragma unroll
+          for (int w = 0; w < 4; ++w) w4[rr][w] = nw[rr][w];
+        }
+        if (gq + 1 < n_tiles) fetch(gq + 1, nw, nl, nd);
         // Buffer b is free once the compute and epilogue warps are done with
         // tile gq - kQBufs and the products reading its Q / dO are complete
         // (the MMA issuer's arrival is a tcgen05.commit for a live tile).
@@ -293,30 +338,6 @@ __global__ void __launch_bounds__(kThreads, 1)
           break;
         }
         const int i0 = qi * kT;
-        // All global loads of the tile (4 rows per lane) are issued before any
-        // of them is used, so their latencies overlap.
-        uint32_t w4[4][4];
-        float l2[4], de[4];
-#pragma unroll
-        for (int rr = 0; rr < 4; ++rr) {
-          const int row = i0 + lane + 32 * rr;
-          const bool in = row < N;
-          const int64_t r64 = static_cast<int64_t>(bh) * N + (in ? row : 0);
-          const uint32_t* mrow = mask + r64 * W + kt * 4;
-          if (vec) {
-            uint4 x = make_uint4(0u, 0u, 0u, 0u);
-            if (in) x = __ldg(reinterpret_cast<const uint4*>(mrow));
-            w4[rr][0] = x.x;
-            w4[rr][1] = x.y;
-            w4[rr][2] = x.z;
-            w4[rr][3] = x.w;
-          } else {
-#pragma unroll
-            for (int w = 0; w < 4; ++w) w4[rr][w] = (in && kt * 4 + w < W) ? __ldg(mrow + w) : 0u;
-          }
-          l2[rr] = in ? __ldg(lse + r64) : 0.f;
-          de[rr] = in ? __ldg(delta + r64) : 0.f;
-        }
         uint32_t any = 0u;
 #pragma unroll
         for (int rr = 0; rr < 4; ++rr) {
