@@ -23,7 +23,8 @@
 //                        MMA  dV += P^T dO, dK += dS^T Q  (A from TMEM)
 //                             dQ_part = dS K              (A from shared memory, M-major)
 //                        dQ_part * scale is added into an FP32 accumulator in
-//                        global memory (red.global.add.v4.f32)
+//                        global memory (staged in shared memory, TMA bulk
+//                        reduce-add)
 //   bwd_dq_convert_kernel  FP32 accumulator -> dq in the input dtype
 //
 // Warps (320 threads): 0-3 compute (thread t <-> TMEM lane t; P^T and dS^T),
@@ -78,10 +79,14 @@ struct BwdCfg {
   static constexpr int kOffMask = kOffDS + 2 * kT * 128;
   static constexpr int kOffLse = kOffMask + kQBufs * 4 * kT * 4;
   static constexpr int kOffDelta = kOffLse + kQBufs * kT * 4;
-  static constexpr int kOffCtl = kOffDelta + kQBufs * kT * 4;
+  // dQ_part staging for the bulk reduce: 8 KiB per epilogue warp (its 32 rows
+  // as two 4 KiB boxes of 32 FP32 columns, 128-byte swizzle); D = 128 stages
+  // its 128 columns in two passes.
+  static constexpr int kOffDQ = (kOffDelta + kQBufs * kT * 4 + 1023) / 1024 * 1024;
+  static constexpr int kOffCtl = kOffDQ + 4 * 8192;
   // Above half of the SM's shared memory, so one CTA holds an SM (its TMEM
   // allocation takes all 512 columns).
-  static constexpr size_t kSmemBytes = 168 * 1024;
+  static constexpr size_t kSmemBytes = 200 * 1024;
 };
 
 struct BwdCtl {
@@ -102,7 +107,8 @@ struct BwdCtl {
 };
 
 // Shared memory: K[kKVBufs] | V[kKVBufs] | Q[kQBufs] | dO[kQBufs] | dS | mask
-// words [kQBufs][4][128] | lse2 [kQBufs][128] | Delta [kQBufs][128] | control.
+// words [kQBufs][4][128] | lse2 [kQBufs][128] | Delta [kQBufs][128] | dQ
+// staging [4 warps][2][32][32] FP32 | control.
 static_assert(BwdCfg<64>::kOffCtl + sizeof(BwdCtl) <= BwdCfg<64>::kSmemBytes, "shared memory layout");
 static_assert(BwdCfg<128>::kOffCtl + sizeof(BwdCtl) <= BwdCfg<128>::kSmemBytes, "shared memory layout");
 
@@ -130,11 +136,6 @@ __device__ __forceinline__ float2 unpack2(uint32_t x) {
   } else {
     return __half22float2(*reinterpret_cast<__half2*>(&x));
   }
-}
-
-__device__ __forceinline__ void red_add_v4(float* dst, float a, float b, float c, float d) {
-  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst), "f"(a), "f"(b), "f"(c), "f"(d)
-               : "memory");
 }
 
 // Bits of packed-mask word cw of a row that address columns < N.
@@ -181,8 +182,8 @@ template <int D, bool BF16>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
-                    const uint32_t* __restrict__ mask, const float* __restrict__ lse,
-                    const float* __restrict__ delta, float* __restrict__ dq_acc, uint16_t* __restrict__ dk,
+                    const __grid_constant__ CUtensorMap tm_dq, const uint32_t* __restrict__ mask,
+                    const float* __restrict__ lse, const float* __restrict__ delta, uint16_t* __restrict__ dk,
                     uint16_t* __restrict__ dv, int N, int W, int KT, int QT, int total_items, int vec, float scale,
                     uint32_t* err_word, uint64_t timeout_ns) {
   using C = BwdCfg<D>;
@@ -253,6 +254,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tm_k);
       tma_prefetch_desc(&tm_v);
       tma_prefetch_desc(&tm_do);
+      tma_prefetch_desc(&tm_dq);
     }
     bool ok = true;
     int gq = 0;
@@ -571,6 +573,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     } else {
       // ============================================================== epilogue
+      uint8_t* s_dq = smem + C::kOffDQ + (warp & 3) * 8192;
       for (int j = 0; ok && j < n_items; ++j) {
         const int item = static_cast<int>(blockIdx.x) + j * G;
         const int bh = item / KT;
@@ -586,19 +589,39 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = wait_all(ctl.dq_full, lt & 1);
           if (!ok) break;
           // dQ_part row t = query row qi*128 + t: all of it into registers,
-          // TMEM released, then scaled and added into the accumulator.
+          // TMEM released, then scaled, staged (this warp's 32 rows) and added
+          // into the FP32 accumulator by TMA bulk reduce-adds, 64 columns per
+          // pass.  A box starting at or past row N has nothing to add; the
+          // rows of a box past N are clipped by the TMA unit.
           float u[D];
 #pragma unroll
           for (int h = 0; h < D / 32; ++h) tmem_ld32f(t_lane + C::col_dq(h >> 1) + (h & 1) * 32, u + 32 * h);
           tmem_wait_ld();
           arrive_warp(ctl.dq_free);
-          const int row = qi * kT + t;
-          if (row < N) {
-            float* dst = dq_acc + (static_cast<int64_t>(bh) * N + row) * D;
+          const int row0 = qi * kT + (warp & 3) * 32;
 #pragma unroll
-            for (int q4 = 0; q4 < D / 4; ++q4)
-              red_add_v4(dst + 4 * q4, u[4 * q4] * scale, u[4 * q4 + 1] * scale, u[4 * q4 + 2] * scale,
-                         u[4 * q4 + 3] * scale);
+          for (int pass = 0; pass < D / 64; ++pass) {
+            // This warp's staging area is free once its previous reduce-adds have read it.
+            if (lane == 0) bulk_wait_group_read0();
+            __syncwarp();
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              uint8_t* srow = s_dq + h * 4096 + lane * 128;
+#pragma unroll
+              for (int c = 0; c < 8; ++c) {
+                const float* x = u + 64 * pass + 32 * h + 4 * c;
+                *reinterpret_cast<float4*>(srow + ((c ^ (lane & 7)) * 16)) =
+                    make_float4(x[0] * scale, x[1] * scale, x[2] * scale, x[3] * scale);
+              }
+            }
+            fence_proxy_async_smem();  // staged by every lane, read by the TMA unit
+            __syncwarp();
+            if (lane == 0 && row0 < N) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h)
+                tma_reduce_add_3d(&tm_dq, smem_u32(s_dq + h * 4096), (2 * pass + h) * 32, row0, bh);
+              bulk_commit_group();
+            }
           }
           ++lt;
           ++item_lt;
@@ -636,6 +659,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         arrive_warp(ctl.acc_free);
       }
+      // The reduce-adds must finish (and stop reading shared memory) before the CTA exits.
+      if (lane == 0) bulk_wait_group0();
     }
     if (!ok && lane == 0) fail();
   }
@@ -660,9 +685,10 @@ int launch(const BwdParams& p, const char** msg) {
     *msg = "backward: batch*heads too large";
     return kErrArg;
   }
-  CUtensorMap mq, mk, mv, mdo;
+  CUtensorMap mq, mk, mv, mdo, mdq;
   if (!make_tensor_map_3d(&mq, p.q, p.dtype, D, BH, N, kT) || !make_tensor_map_3d(&mk, p.k, p.dtype, D, BH, N, kT) ||
-      !make_tensor_map_3d(&mv, p.v, p.dtype, D, BH, N, kT) || !make_tensor_map_3d(&mdo, p.dout, p.dtype, D, BH, N, kT)) {
+      !make_tensor_map_3d(&mv, p.v, p.dtype, D, BH, N, kT) || !make_tensor_map_3d(&mdo, p.dout, p.dtype, D, BH, N, kT) ||
+      !make_tensor_map_3d_f32(&mdq, p.dq_accum, D, BH, N, 32)) {
     *msg = "backward: cuTensorMapEncodeTiled failed (pointer alignment or driver entry point)";
     return kErrCuda;
   }
@@ -701,7 +727,7 @@ int launch(const BwdParams& p, const char** msg) {
     const int64_t items = BH * KT;
     const int64_t grid = items < sms[dev] ? items : sms[dev];
     kern<<<static_cast<unsigned>(grid), kThreads, C::kSmemBytes, p.stream>>>(
-        mq, mk, mv, mdo, p.mask, p.lse, p.delta, p.dq_accum, static_cast<uint16_t*>(p.dk),
+        mq, mk, mv, mdo, mdq, p.mask, p.lse, p.delta, static_cast<uint16_t*>(p.dk),
         static_cast<uint16_t*>(p.dv), static_cast<int>(N), static_cast<int>(W), static_cast<int>(KT),
         static_cast<int>(QT), static_cast<int>(items), vec, p.scale, p.err_word, p.timeout_ns);
     e = cudaGetLastError();

@@ -81,6 +81,9 @@ int launch_attn_bwd(const BwdParams& p, const char** msg);
 // tensor: boxes of 64 head dims (one 128-byte swizzle span) by `rows` rows,
 // 128-byte swizzle (tma_map.cu).
 bool make_tensor_map_3d(CUtensorMap* m, const void* ptr, int dtype, int64_t D, int64_t BH, int64_t N, int rows);
+// The same view of a contiguous FP32 [BH, N, D] tensor: boxes of 32 elements
+// (128 bytes) by `rows` rows, 128-byte swizzle (tma_map.cu).
+bool make_tensor_map_3d_f32(CUtensorMap* m, const void* ptr, int64_t D, int64_t BH, int64_t N, int rows);
 
 // Launches `kern` with programmatic stream serialisation: its CTAs may start
 // (and run their set-up) while the previous kernel in the stream finishes;
