@@ -27,12 +27,14 @@
 //                        reduce-add)
 //   bwd_dq_convert_kernel  FP32 accumulator -> dq in the input dtype
 //
-// Warps (320 threads): 0-3 compute (thread t <-> TMEM lane t; P^T and dS^T),
-// 4 loader (TMA of K, V, Q, dO; mask words, LSE and Delta of the query tile
-// staged in shared memory), 5 MMA issuer and TMEM owner, 6-9 epilogue (dQ_part
-// of each live tile into the FP32 accumulator, dK and dV of each item; warp w
-// reads TMEM lanes 32(w%4)..+31), so the epilogues of one tile overlap the
-// element-wise work of the next.  TMEM layout per head dim: see BwdCfg.
+// Warps (E = 8 element-wise warps for D = 64, 4 for D = 128): 0..E-1 compute
+// (P^T and dS^T; thread <-> TMEM lane 32(w%4) + lane, warp w takes 32-query
+// chunks of the tile by w/4), E loader (TMA of K, V, Q, dO; mask words, LSE and
+// Delta of the query tile staged in shared memory), E+1 MMA issuer and TMEM
+// owner, E+2..E+5 epilogue (dQ_part of each live tile into the FP32
+// accumulator, dK and dV of each item; warp w reads TMEM lanes 32(w%4)..+31),
+// so the epilogues of one tile overlap the element-wise work of the next.
+// TMEM layout per head dim: see BwdCfg.
 // Every wait is bounded and reports through the device error word.
 #include <cfloat>
 #include <cuda_bf16.h>
@@ -45,7 +47,6 @@ namespace sma {
 namespace {
 
 constexpr int kT = 128;  // query rows and keys per tile
-constexpr int kThreads = 320;
 constexpr int kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256;
 constexpr float kLog2e = 1.44269504088896340736f;
@@ -62,6 +63,23 @@ constexpr int kMaxDevices = 64;
 template <int D>
 struct BwdCfg {
   static_assert(D == 64 || D == 128, "head dim");
+  // Element-wise warps.  D = 64 runs two per TMEM lane quadrant, each taking
+  // half of a tile's 128 query columns; the second half's packed P^T / dS^T
+  // go to the free columns [448, 512), so neither warp writes columns the
+  // other still reads.  D = 128 has no free columns and runs one per quadrant
+  // (packing in place, chunk by chunk).
+  static constexpr int kEwWarps = D == 64 ? 8 : 4;
+  static constexpr int kChunksPerWarp = 16 / kEwWarps;  // 32-query chunks of a tile per element-wise warp
+  static constexpr int kLoaderWarp = kEwWarps;
+  static constexpr int kMmaWarp = kEwWarps + 1;
+  static constexpr int kThreads = (kEwWarps + 6) * 32;
+  // Packed P^T / dS^T of 32-query chunk c (16 columns each).
+  __host__ __device__ static constexpr uint32_t col_p(int c) {
+    return (D == 64 && c >= 2) ? 448u + (c - 2) * 16u : kColS + c * 16u;
+  }
+  __host__ __device__ static constexpr uint32_t col_ds(int c) {
+    return (D == 64 && c >= 2) ? 480u + (c - 2) * 16u : kColDP + c * 16u;
+  }
   static constexpr int kDChunks = D / 64;
   static constexpr int kTileBytes = kT * D * 2;  // 16 / 32 KiB
   static constexpr int kKVBufs = D == 64 ? 2 : 1;
@@ -179,7 +197,7 @@ __global__ void __launch_bounds__(256) bwd_dq_convert_kernel(const float4* __res
 }
 
 template <int D, bool BF16>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                     const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_do,
                     const __grid_constant__ CUtensorMap tm_dq, const uint32_t* __restrict__ mask,
@@ -218,12 +236,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(smem_u32(&ctl.kv_full[b]), 1);
       mbar_init(smem_u32(&ctl.kv_free[b]), 1);
       mbar_init(smem_u32(&ctl.ld_full[b]), 1);
-      mbar_init(smem_u32(&ctl.tile_free[b]), 9);  // 4 compute + 4 epilogue warps + the MMA issuer
+      mbar_init(smem_u32(&ctl.tile_free[b]), C::kEwWarps + 5);  // compute + 4 epilogue warps + the MMA issuer
       ctl.live[b] = 0;
     }
     mbar_init(smem_u32(&ctl.acc_free), 4);
     mbar_init(smem_u32(&ctl.st_full), 1);
-    mbar_init(smem_u32(&ctl.p_full), 4);
+    mbar_init(smem_u32(&ctl.p_full), C::kEwWarps);
     mbar_init(smem_u32(&ctl.pt_free), 1);
     mbar_init(smem_u32(&ctl.dq_full), 1);
     mbar_init(smem_u32(&ctl.dq_free), 4);
@@ -232,7 +250,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
     fence_proxy_async_smem();
   }
-  if (warp == 5) {
+  if (warp == C::kMmaWarp) {
     tmem_alloc(smem_u32(&ctl.tmem_base), kTmemCols);
     tmem_relinquish();
   }
@@ -247,7 +265,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     atomicOr(err_word, kDevErrTimeout);
   };
 
-  if (warp == 4) {
+  if (warp == C::kLoaderWarp) {
     // ================================================================ loader
     if (lane == 0) {
       tma_prefetch_desc(&tm_q);
@@ -384,7 +402,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int g = last_copy - kQBufs + 1; g <= last_copy; ++g)
         if (g >= 0) mbar_wait_bounded(smem_u32(&ctl.ld_full[g % kQBufs]), (g / kQBufs) & 1, &zero, timeout_ns);
     }
-  } else if (warp == 5) {
+  } else if (warp == C::kMmaWarp) {
     // ================================================================ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_f16(kT, kT, BF16 ? 1 : 0, 0);       // S^T, dP^T (M = keys)
@@ -453,11 +471,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           // whose 64-dim chunks (D = 128) are kT * 128 bytes apart.
 #pragma unroll
           for (int kk = 0; kk < kT / 16; ++kk)
-            mma_ts(tmem + kColDV, tmem + kColS + kk * 8, smem_desc_sw128(sDO + kk * 2048, kT * 128, 1024), idesc_kv,
+            mma_ts(tmem + kColDV, tmem + C::col_p(kk >> 1) + (kk & 1) * 8, smem_desc_sw128(sDO + kk * 2048, kT * 128, 1024),
+                   idesc_kv,
                    (item_lt > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
           for (int kk = 0; kk < kT / 16; ++kk)
-            mma_ts(tmem + C::kColDK, tmem + kColDP + kk * 8, smem_desc_sw128(sQ + kk * 2048, kT * 128, 1024),
+            mma_ts(tmem + C::kColDK, tmem + C::col_ds(kk >> 1) + (kk & 1) * 8,
+                   smem_desc_sw128(sQ + kk * 2048, kT * 128, 1024),
                    idesc_kv, (item_lt > 0 || kk > 0) ? 1u : 0u);
           if constexpr (C::kDQApart) {
             mma_commit(smem_u32(&ctl.pt_free));
@@ -510,7 +530,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool ok = true;
     int gq = 0;
     uint32_t lt = 0;
-    if (warp < 4) {
+    if (warp < C::kEwWarps) {
       // ============================================================== compute
       const float c2 = scale * kLog2e;
       const int my_word = (t >> 5) * kT;  // the word holding this key, for each query row
@@ -527,7 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = wait_all(ctl.st_full, lt & 1);
           if (!ok) break;
 #pragma unroll 1
-          for (int c = 0; c < kT / 32; ++c) {
+          for (int c = (warp >> 2) * C::kChunksPerWarp; c < ((warp >> 2) + 1) * C::kChunksPerWarp; ++c) {
             float s[32], dp[32];
             tmem_ld32f(t_lane + kColS + c * 32, s);
             tmem_ld32f(t_lane + kColDP + c * 32, dp);
@@ -551,10 +571,11 @@ __global__ void __launch_bounds__(kThreads, 1)
               dw[e / 2] = pack2<BF16>(ds[0], ds[1]);
               dw[e / 2 + 1] = pack2<BF16>(ds[2], ds[3]);
             }
-            // P^T and dS^T over the S^T / dP^T columns already read (chunk c
-            // writes columns 16c.., whose values belong to chunks <= c).
-            tmem_st16(t_lane + kColS + c * 16, pw);
-            tmem_st16(t_lane + kColDP + c * 16, dw);
+            // P^T and dS^T packed: in place over S^T / dP^T columns this warp
+            // has already read (chunk c writes columns 16c.., whose values
+            // belong to chunks <= c), or into the free columns (see col_p).
+            tmem_st16(t_lane + C::col_p(c), pw);
+            tmem_st16(t_lane + C::col_ds(c), dw);
             // dS for the dQ MMA: row t of the M-major operand, queries
             // 32c .. 32c+31 = 16-byte chunks 4(c&1) .. +3 of 64-query chunk c/2,
             // 128-byte swizzle (chunk index XOR row % 8).
@@ -667,7 +688,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == C::kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem, kTmemCols);
   }
@@ -726,7 +747,7 @@ int launch(const BwdParams& p, const char** msg) {
     // One CTA per SM (168 KB of shared memory and all 512 TMEM columns each).
     const int64_t items = BH * KT;
     const int64_t grid = items < sms[dev] ? items : sms[dev];
-    kern<<<static_cast<unsigned>(grid), kThreads, C::kSmemBytes, p.stream>>>(
+    kern<<<static_cast<unsigned>(grid), C::kThreads, C::kSmemBytes, p.stream>>>(
         mq, mk, mv, mdo, mdq, p.mask, p.lse, p.delta, static_cast<uint16_t*>(p.dk),
         static_cast<uint16_t*>(p.dv), static_cast<int>(N), static_cast<int>(W), static_cast<int>(KT),
         static_cast<int>(QT), static_cast<int>(items), vec, p.scale, p.err_word, p.timeout_ns);
