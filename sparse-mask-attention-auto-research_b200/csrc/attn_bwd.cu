@@ -86,25 +86,32 @@ struct BwdCfg {
   static constexpr int kQBufs = D == 64 ? 2 : 1;
   static constexpr uint32_t kColDK = kColDV + D;
   __host__ __device__ static constexpr uint32_t col_dq(int h) { return D == 64 ? 384u : (h == 0 ? 64u : 192u); }
-  // The next tile's S^T / dP^T may be issued while the epilogue warps still
-  // read this tile's dQ_part only when the two do not share TMEM columns.
+  // With dQ_part in its own TMEM columns (D = 64), the next tile's S^T / dP^T
+  // may be issued while the epilogue warps still read this tile's dQ_part, and
+  // a tile's dQ_part product is issued after the next tile's S^T / dP^T, so
+  // the element-wise warps do not wait behind it in the tensor pipe; dS is
+  // then double-buffered in shared memory.
   static constexpr bool kDQApart = D == 64;
+  static constexpr int kDSBufs = kDQApart ? 2 : 1;
+  // dQ_part staging boxes (4 KiB: 32 rows of 32 FP32 columns) per epilogue warp.
+  static constexpr int kStageBoxes = D == 64 ? 1 : 2;
   static constexpr int kOffK = 0;
   static constexpr int kOffV = kKVBufs * kTileBytes;
   static constexpr int kOffQ = 2 * kKVBufs * kTileBytes;
   static constexpr int kOffDO = kOffQ + kQBufs * kTileBytes;
-  static constexpr int kOffDS = kOffDO + kQBufs * kTileBytes;  // two 16 KiB M-major chunks of 64 queries
-  static constexpr int kOffMask = kOffDS + 2 * kT * 128;
+  // dS buffers: two 16 KiB M-major chunks of 64 queries each.
+  static constexpr int kOffDS = kOffDO + kQBufs * kTileBytes;
+  static constexpr int kOffMask = kOffDS + kDSBufs * 2 * kT * 128;
   static constexpr int kOffLse = kOffMask + kQBufs * 4 * kT * 4;
   static constexpr int kOffDelta = kOffLse + kQBufs * kT * 4;
-  // dQ_part staging for the bulk reduce: 8 KiB per epilogue warp (its 32 rows
-  // as two 4 KiB boxes of 32 FP32 columns, 128-byte swizzle); D = 128 stages
-  // its 128 columns in two passes.
+  // dQ_part staging for the bulk reduce: kStageBoxes 4 KiB boxes per epilogue
+  // warp (its 32 rows by 32 FP32 columns, 128-byte swizzle), reused for the
+  // D/32 column boxes of a tile in turn.
   static constexpr int kOffDQ = (kOffDelta + kQBufs * kT * 4 + 1023) / 1024 * 1024;
-  static constexpr int kOffCtl = kOffDQ + 4 * 8192;
+  static constexpr int kOffCtl = kOffDQ + 4 * kStageBoxes * 4096;
   // Above half of the SM's shared memory, so one CTA holds an SM (its TMEM
   // allocation takes all 512 columns).
-  static constexpr size_t kSmemBytes = 200 * 1024;
+  static constexpr size_t kSmemBytes = D == 64 ? 216 * 1024 : 200 * 1024;
 };
 
 struct BwdCtl {
@@ -124,9 +131,9 @@ struct BwdCtl {
   uint32_t abort_flag;
 };
 
-// Shared memory: K[kKVBufs] | V[kKVBufs] | Q[kQBufs] | dO[kQBufs] | dS | mask
-// words [kQBufs][4][128] | lse2 [kQBufs][128] | Delta [kQBufs][128] | dQ
-// staging [4 warps][2][32][32] FP32 | control.
+// Shared memory: K[kKVBufs] | V[kKVBufs] | Q[kQBufs] | dO[kQBufs] | dS[kDSBufs]
+// | mask words [kQBufs][4][128] | lse2 [kQBufs][128] | Delta [kQBufs][128] |
+// dQ staging [4 warps][kStageBoxes][32][32] FP32 | control.
 static_assert(BwdCfg<64>::kOffCtl + sizeof(BwdCtl) <= BwdCfg<64>::kSmemBytes, "shared memory layout");
 static_assert(BwdCfg<128>::kOffCtl + sizeof(BwdCtl) <= BwdCfg<128>::kSmemBytes, "shared memory layout");
 
@@ -408,10 +415,40 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
       constexpr uint32_t idesc_s = make_idesc_f16(kT, kT, BF16 ? 1 : 0, 0);       // S^T, dP^T (M = keys)
       constexpr uint32_t idesc_kv = make_idesc_f16(kT, D, BF16 ? 1 : 0, 1);       // dV, dK (B M/N-major)
       constexpr uint32_t idesc_q = make_idesc_f16(kT, 64, BF16 ? 1 : 0, 1, 1);    // dQ half (A and B M/N-major)
-      const uint32_t sDS = base + C::kOffDS;
       bool ok = true;
       int gq = 0;
       uint32_t lt = 0;
+      // dQ_part = dS K of live tile L (K of its item at sKL) in 64-dim halves:
+      // 16 keys per step; dS's two 64-query chunks are kT * 128 bytes apart,
+      // as are K's 64-dim chunks.  With dQ_part in its own columns, the
+      // epilogue warps must have read tile L-1's first.
+      auto issue_dq = [&](uint32_t L, uint32_t sKL) -> bool {
+        if (C::kDQApart && L > 0 && !mbar_wait_bounded(smem_u32(&ctl.dq_free), (L - 1) & 1, abort_flag, timeout_ns))
+          return false;
+        tc_fence_after();
+        const uint32_t sDS = base + C::kOffDS + (L % C::kDSBufs) * (2 * kT * 128);
+#pragma unroll
+        for (int h = 0; h < C::kDChunks; ++h)
+#pragma unroll
+          for (int kk = 0; kk < kT / 16; ++kk)
+            mma_ss(tmem + C::col_dq(h), smem_desc_sw128(sDS + kk * 2048, kT * 128, 1024),
+                   smem_desc_sw128(sKL + h * (kT * 128) + kk * 2048, kT * 128, 1024), idesc_q, kk > 0 ? 1u : 0u);
+        mma_commit(smem_u32(&ctl.dq_full));
+        return true;
+      };
+      // D = 64: the live tile whose dQ_part is still to be issued, the K it
+      // reads, its item, and (once that item has ended) the K/V buffer to
+      // release after it.
+      int pend = -1, pend_item = -1, pend_kv = -1;
+      uint32_t pend_sk = 0;
+      auto flush = [&]() -> bool {
+        if (pend < 0) return true;
+        if (!issue_dq(static_cast<uint32_t>(pend), pend_sk)) return false;
+        if (pend_kv >= 0) mma_commit(smem_u32(&ctl.kv_free[pend_kv]));
+        pend = -1;
+        pend_kv = -1;
+        return true;
+      };
       for (int j = 0; ok && j < n_items; ++j) {
         const int bkv = j % kKVBufs;
         const uint32_t sK = base + C::kOffK + bkv * kTileBytes, sV = base + C::kOffV + bkv * kTileBytes;
@@ -428,6 +465,14 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
             break;
           }
           if (ctl.live[b] == 0u) {
+            // D = 64: a pending dQ_part is issued in the slot of the very next
+            // tile, live or not.  (The epilogue warps wait for it before they
+            // release later staging buffers, so it may not wait for a later
+            // live tile.)
+            if (C::kDQApart && !flush()) {
+              ok = false;
+              break;
+            }
             mbar_arrive(smem_u32(&ctl.tile_free[b]));
             continue;
           }
@@ -454,9 +499,14 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
             mma_ss(tmem + kColDP, smem_desc_sw128(sV + off, 16, 1024), smem_desc_sw128(sDO + off, 16, 1024), idesc_s,
                    kk > 0 ? 1u : 0u);
           }
-          // st_full also covers every earlier product, so dQ_part of the
-          // previous tile has read dS from shared memory before it is rewritten.
+          // st_full also covers every earlier product, so the dQ_part that
+          // last read this tile's dS buffer has done so before it is rewritten.
           mma_commit(smem_u32(&ctl.st_full));
+          // D = 64: the previous live tile's dQ_part, behind this tile's S^T / dP^T.
+          if (C::kDQApart && !flush()) {
+            ok = false;
+            break;
+          }
           // P^T / dS^T of this tile; before the first dV / dK product of item
           // j, the epilogue warps must have read item j-1's dV / dK.
           if (!mbar_wait_bounded(smem_u32(&ctl.p_full), lt & 1, abort_flag, timeout_ns) ||
@@ -472,39 +522,47 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
 #pragma unroll
           for (int kk = 0; kk < kT / 16; ++kk)
             mma_ts(tmem + kColDV, tmem + C::col_p(kk >> 1) + (kk & 1) * 8, smem_desc_sw128(sDO + kk * 2048, kT * 128, 1024),
-                   idesc_kv,
-                   (item_lt > 0 || kk > 0) ? 1u : 0u);
+                   idesc_kv, (item_lt > 0 || kk > 0) ? 1u : 0u);
 #pragma unroll
           for (int kk = 0; kk < kT / 16; ++kk)
             mma_ts(tmem + C::kColDK, tmem + C::col_ds(kk >> 1) + (kk & 1) * 8,
-                   smem_desc_sw128(sQ + kk * 2048, kT * 128, 1024),
-                   idesc_kv, (item_lt > 0 || kk > 0) ? 1u : 0u);
+                   smem_desc_sw128(sQ + kk * 2048, kT * 128, 1024), idesc_kv, (item_lt > 0 || kk > 0) ? 1u : 0u);
           if constexpr (C::kDQApart) {
             mma_commit(smem_u32(&ctl.pt_free));
-            // dQ_part in its own columns: the previous tile's must have been read.
-            if (lt > 0 && !mbar_wait_bounded(smem_u32(&ctl.dq_free), (lt - 1) & 1, abort_flag, timeout_ns)) {
+            // Q / dO of the staging buffer are released when dV / dK complete.
+            mma_commit(smem_u32(&ctl.tile_free[b]));
+            pend = static_cast<int>(lt);
+            pend_item = j;
+            pend_sk = sK;
+          } else {
+            if (!issue_dq(lt, sK)) {
               ok = false;
               break;
             }
-            tc_fence_after();
+            // Q / dO of the staging buffer are released when these products complete.
+            mma_commit(smem_u32(&ctl.tile_free[b]));
           }
-          // dQ_part = dS K in 64-dim halves: 16 keys per step; dS's two
-          // 64-query chunks are kT * 128 bytes apart, as are K's 64-dim chunks.
-#pragma unroll
-          for (int h = 0; h < C::kDChunks; ++h)
-#pragma unroll
-            for (int kk = 0; kk < kT / 16; ++kk)
-              mma_ss(tmem + C::col_dq(h), smem_desc_sw128(sDS + kk * 2048, kT * 128, 1024),
-                     smem_desc_sw128(sK + h * (kT * 128) + kk * 2048, kT * 128, 1024), idesc_q, kk > 0 ? 1u : 0u);
-          mma_commit(smem_u32(&ctl.dq_full));
-          // The staging buffer's Q / dO are released when these products complete.
-          mma_commit(smem_u32(&ctl.tile_free[b]));
           ++lt;
           ++item_lt;
         }
-        // K/V buffer bkv may be refilled once this item's MMAs are complete.
-        if (ok) mma_commit(smem_u32(&ctl.kv_free[bkv]));
+        if (!ok) break;
+        // K/V buffer bkv may be refilled once this item's products are
+        // complete.  D = 64: a dQ_part pending from this item (its last tile
+        // was live) releases bkv when it is issued, in the next tile's slot.
+        if constexpr (C::kDQApart) {
+          if (pend >= 0 && pend_item < j && !flush()) {
+            ok = false;
+            break;
+          }
+          if (pend >= 0)
+            pend_kv = bkv;
+          else
+            mma_commit(smem_u32(&ctl.kv_free[bkv]));
+        } else {
+          mma_commit(smem_u32(&ctl.kv_free[bkv]));
+        }
       }
+      if (ok && C::kDQApart && !flush()) ok = false;
       if (!ok) fail();
       // Every MMA this thread issued must complete before TMEM is released.
       mma_commit(smem_u32(&ctl.drain));
@@ -579,7 +637,7 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
             // dS for the dQ MMA: row t of the M-major operand, queries
             // 32c .. 32c+31 = 16-byte chunks 4(c&1) .. +3 of 64-query chunk c/2,
             // 128-byte swizzle (chunk index XOR row % 8).
-            uint8_t* drow = smem + C::kOffDS + (c >> 1) * (kT * 128) + t * 128;
+            uint8_t* drow = smem + C::kOffDS + (lt % C::kDSBufs) * (2 * kT * 128) + (c >> 1) * (kT * 128) + t * 128;
 #pragma unroll
             for (int q = 0; q < 4; ++q)
               *reinterpret_cast<uint4*>(drow + ((((c & 1) * 4 + q) ^ (t & 7)) * 16)) =
@@ -594,7 +652,7 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
       }
     } else {
       // ============================================================== epilogue
-      uint8_t* s_dq = smem + C::kOffDQ + (warp & 3) * 8192;
+      uint8_t* s_dq = smem + C::kOffDQ + (warp & 3) * (C::kStageBoxes * 4096);
       for (int j = 0; ok && j < n_items; ++j) {
         const int item = static_cast<int>(blockIdx.x) + j * G;
         const int bh = item / KT;
@@ -611,9 +669,9 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
           if (!ok) break;
           // dQ_part row t = query row qi*128 + t: all of it into registers,
           // TMEM released, then scaled, staged (this warp's 32 rows) and added
-          // into the FP32 accumulator by TMA bulk reduce-adds, 64 columns per
-          // pass.  A box starting at or past row N has nothing to add; the
-          // rows of a box past N are clipped by the TMA unit.
+          // into the FP32 accumulator by TMA bulk reduce-adds, kStageBoxes
+          // boxes of 32 columns per pass.  A box starting at or past row N has
+          // nothing to add; the rows of a box past N are clipped by the TMA unit.
           float u[D];
 #pragma unroll
           for (int h = 0; h < D / 32; ++h) tmem_ld32f(t_lane + C::col_dq(h >> 1) + (h & 1) * 32, u + 32 * h);
@@ -621,16 +679,16 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
           arrive_warp(ctl.dq_free);
           const int row0 = qi * kT + (warp & 3) * 32;
 #pragma unroll
-          for (int pass = 0; pass < D / 64; ++pass) {
+          for (int pass = 0; pass < D / (32 * C::kStageBoxes); ++pass) {
             // This warp's staging area is free once its previous reduce-adds have read it.
             if (lane == 0) bulk_wait_group_read0();
             __syncwarp();
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
+            for (int h = 0; h < C::kStageBoxes; ++h) {
               uint8_t* srow = s_dq + h * 4096 + lane * 128;
 #pragma unroll
               for (int c = 0; c < 8; ++c) {
-                const float* x = u + 64 * pass + 32 * h + 4 * c;
+                const float* x = u + 32 * (C::kStageBoxes * pass + h) + 4 * c;
                 *reinterpret_cast<float4*>(srow + ((c ^ (lane & 7)) * 16)) =
                     make_float4(x[0] * scale, x[1] * scale, x[2] * scale, x[3] * scale);
               }
@@ -639,8 +697,8 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
             __syncwarp();
             if (lane == 0 && row0 < N) {
 #pragma unroll
-              for (int h = 0; h < 2; ++h)
-                tma_reduce_add_3d(&tm_dq, smem_u32(s_dq + h * 4096), (2 * pass + h) * 32, row0, bh);
+              for (int h = 0; h < C::kStageBoxes; ++h)
+                tma_reduce_add_3d(&tm_dq, smem_u32(s_dq + h * 4096), (C::kStageBoxes * pass + h) * 32, row0, bh);
               bulk_commit_group();
             }
           }
