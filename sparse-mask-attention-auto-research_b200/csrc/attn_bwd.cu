@@ -423,9 +423,10 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
       // as are K's 64-dim chunks.  With dQ_part in its own columns, the
       // epilogue warps must have read tile L-1's first.
       auto issue_dq = [&](uint32_t L, uint32_t sKL) -> bool {
-        if (C::kDQApart && L > 0 && !mbar_wait_bounded(smem_u32(&ctl.dq_free), (L - 1) & 1, abort_flag, timeout_ns))
-          return false;
-        tc_fence_after();
+        if constexpr (C::kDQApart) {
+          if (L > 0 && !mbar_wait_bounded(smem_u32(&ctl.dq_free), (L - 1) & 1, abort_flag, timeout_ns)) return false;
+          tc_fence_after();
+        }
         const uint32_t sDS = base + C::kOffDS + (L % C::kDSBufs) * (2 * kT * 128);
 #pragma unroll
         for (int h = 0; h < C::kDChunks; ++h)
