@@ -11,7 +11,8 @@
 //   dQ  = scale * dS K,   dK = scale * dS^T Q
 //
 // Kernels (one stream, in order):
-//   bwd_delta_kernel   Delta from dO and O (FP32), 8 threads per row
+//   bwd_delta_kernel   Delta from dO and O (FP32), D/8 threads per row; also
+//                      zeroes the FP32 dQ accumulator
 //   attn_bwd_kernel    persistent, one CTA per SM looping over the items
 //                      (batch*head, 128-key tile).  Per item K and V stay in
 //                      shared memory, dK and dV accumulate in TMEM, and the
@@ -170,15 +171,21 @@ __device__ __forceinline__ uint32_t valid_bits(int cw, int N) {
 }
 
 // Delta[row] = sum_d dO[row, d] * O[row, d] in FP32; D/8 threads per row, one
-// 16-byte load of each operand per thread.
+// 16-byte load of each operand per thread.  Each thread also zeroes the 8 FP32
+// dQ accumulator elements of its 8 (row, d), which the backward kernel then
+// reduce-adds into (one pass instead of a separate memset).
 template <int D, bool BF16>
 __global__ void __launch_bounds__(256) bwd_delta_kernel(const uint4* __restrict__ dout, const uint4* __restrict__ out,
-                                                         float* __restrict__ delta, int64_t rows) {
+                                                         float* __restrict__ delta, float4* __restrict__ dq_acc,
+                                                         int64_t rows) {
   constexpr int kPerRow = D / 8;
   const int64_t gid = static_cast<int64_t>(blockIdx.x) * 256 + threadIdx.x;
   const int64_t row = gid / kPerRow;
   float acc = 0.f;
   if (row < rows) {
+    const float4 zero = make_float4(0.f, 0.f, 0.f, 0.f);
+    dq_acc[2 * gid] = zero;
+    dq_acc[2 * gid + 1] = zero;
     const uint4 a = __ldg(dout + gid), b = __ldg(out + gid);
     const uint32_t aw[4] = {a.x, a.y, a.z, a.w}, bw[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
@@ -536,12 +543,14 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
             pend_item = j;
             pend_sk = sK;
           } else {
+            // Q / dO of the staging buffer are released when dV / dK complete
+            // (the dQ product reads neither), so the next tile's loads start
+            // while it runs.
+            mma_commit(smem_u32(&ctl.tile_free[b]));
             if (!issue_dq(lt, sK)) {
               ok = false;
               break;
             }
-            // Q / dO of the staging buffer are released when these products complete.
-            mma_commit(smem_u32(&ctl.tile_free[b]));
           }
           ++lt;
           ++item_lt;
@@ -795,15 +804,13 @@ int launch(const BwdParams& p, const char** msg) {
     smem_set[dev] = true;
   }
   const int64_t rows = BH * N;
-  cudaError_t e = cudaMemsetAsync(p.dq_accum, 0, static_cast<size_t>(rows) * D * sizeof(float), p.stream);
-  if (e == cudaSuccess) {
-    bwd_delta_kernel<D, BF16><<<static_cast<unsigned>((rows * (D / 8) + 255) / 256), 256, 0, p.stream>>>(
-        static_cast<const uint4*>(p.dout), static_cast<const uint4*>(p.out), p.delta, rows);
-    e = cudaGetLastError();
-  }
+  bwd_delta_kernel<D, BF16><<<static_cast<unsigned>((rows * (D / 8) + 255) / 256), 256, 0, p.stream>>>(
+      static_cast<const uint4*>(p.dout), static_cast<const uint4*>(p.out), p.delta,
+      reinterpret_cast<float4*>(p.dq_accum), rows);
+  cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) {
     const int vec = (W % 4 == 0 && (reinterpret_cast<uintptr_t>(p.mask) & 15u) == 0) ? 1 : 0;
-    // One CTA per SM (168 KB of shared memory and all 512 TMEM columns each).
+    // One CTA per SM (over half of its shared memory and all 512 TMEM columns each).
     const int64_t items = BH * KT;
     const int64_t grid = items < sms[dev] ? items : sms[dev];
     kern<<<static_cast<unsigned>(grid), C::kThreads, C::kSmemBytes, p.stream>>>(
