@@ -73,7 +73,8 @@ struct BwdCfg {
   static constexpr int kChunksPerWarp = 16 / kEwWarps;  // 32-query chunks of a tile per element-wise warp
   static constexpr int kLoaderWarp = kEwWarps;
   static constexpr int kMmaWarp = kEwWarps + 1;
-  static constexpr int kThreads = (kEwWarps + 6) * 32;
+  static constexpr int kScanWarp = kEwWarps + 6;  // after the 4 epilogue warps
+  static constexpr int kThreads = (kEwWarps + 7) * 32;
   // Packed P^T / dS^T of 32-query chunk c (16 columns each).
   __host__ __device__ static constexpr uint32_t col_p(int c) {
     return (D == 64 && c >= 2) ? 448u + (c - 2) * 16u : kColS + c * 16u;
@@ -115,26 +116,34 @@ struct BwdCfg {
   static constexpr size_t kSmemBytes = D == 64 ? 216 * 1024 : 200 * 1024;
 };
 
+// Items whose live query-tile lists the scanner warp publishes ahead, and
+// words of a list (one bit per 128-row query tile; 16 words cover N <= 65536).
+constexpr int kSlots = 4;
+constexpr int kLiveWords = 16;
+
 struct BwdCtl {
-  uint64_t kv_full[2];    // K and V of an item landed in buffer b
-  uint64_t kv_free[2];    // MMAs of the item in K/V buffer b complete (committed by the MMA issuer)
-  uint64_t acc_free;      // dV and dK of an item read out of TMEM (4 epilogue warps)
-  uint64_t ld_full[2];    // query tile staged in buffer b (Q, dO by TMA; mask, LSE, Delta by the loader warp)
+  uint64_t kv_full[2];    // K and V of a live item landed in buffer b
+  uint64_t kv_free[2];    // products of the live item in K/V buffer b complete (committed by the MMA issuer)
+  uint64_t acc_free;      // dV and dK of a live item read out of TMEM (4 epilogue warps)
+  uint64_t ld_full[2];    // live query tile staged in buffer b (Q, dO by TMA; mask, LSE, Delta by the loader)
   uint64_t st_full;       // S^T and dP^T complete
-  uint64_t p_full;        // P^T, dS^T in TMEM and dS in shared memory (4 compute warps)
+  uint64_t p_full;        // P^T, dS^T in TMEM and dS in shared memory (compute warps)
   uint64_t pt_free;       // dV, dK products of a tile complete (they read P^T / dS^T in TMEM)
   uint64_t dq_full;       // all products of a tile complete (dQ_part in TMEM)
   uint64_t dq_free;       // dQ_part of a tile read out of TMEM (4 epilogue warps)
-  uint64_t tile_free[2];  // compute, epilogue warps and the MMA issuer done with buffer b (9 arrivals)
+  uint64_t tile_free[2];  // compute warps and the MMA issuer done with buffer b
+  uint64_t item_full[kSlots];  // live list of an item published (scanner warp)
+  uint64_t item_free[kSlots];  // every other warp done with that list
   uint64_t drain;
+  uint32_t live_bits[kSlots][kLiveWords];
+  uint32_t n_live[kSlots];
   uint32_t tmem_base;
-  uint32_t live[2];
   uint32_t abort_flag;
 };
 
 // Shared memory: K[kKVBufs] | V[kKVBufs] | Q[kQBufs] | dO[kQBufs] | dS[kDSBufs]
 // | mask words [kQBufs][4][128] | lse2 [kQBufs][128] | Delta [kQBufs][128] |
-// dQ staging [4 warps][kStageBoxes][32][32] FP32 | control.
+// dQ staging [4 warps][kStageBoxes][32][32] FP32 | control (with the live lists).
 static_assert(BwdCfg<64>::kOffCtl + sizeof(BwdCtl) <= BwdCfg<64>::kSmemBytes, "shared memory layout");
 static_assert(BwdCfg<128>::kOffCtl + sizeof(BwdCtl) <= BwdCfg<128>::kSmemBytes, "shared memory layout");
 
@@ -168,6 +177,17 @@ __device__ __forceinline__ float2 unpack2(uint32_t x) {
 __device__ __forceinline__ uint32_t valid_bits(int cw, int N) {
   const int valid = N - cw * 32;
   return valid >= 32 ? 0xFFFFFFFFu : (valid <= 0 ? 0u : ((1u << valid) - 1u));
+}
+
+// Next set bit of a live list from cursor (w, x): the query tile index, or -1.
+__device__ __forceinline__ int next_live_tile(const uint32_t* bits, int& w, uint32_t& x) {
+  while (x == 0u) {
+    if (++w >= kLiveWords) return -1;
+    x = bits[w];
+  }
+  const int b = __ffs(x) - 1;
+  x &= x - 1u;
+  return w * 32 + b;
 }
 
 // Delta[row] = sum_d dO[row, d] * O[row, d] in FP32; D/8 threads per row, one
@@ -238,9 +258,12 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
   const int lane = threadIdx.x & 31;
   // Persistent: CTA c takes items c, c + G, c + 2G, ... of item = batch*head *
   // KT + key tile, so the CTAs running at one time cover the key tiles of a
-  // few heads side by side and share those heads' Q and dO in L2.  Counters
-  // that run over all items of the CTA: j (items; K/V buffer j % kKVBufs), gq
-  // (query tiles; staging buffer gq % kQBufs), lt (live query tiles).
+  // few heads side by side and share those heads' Q and dO in L2.  The scanner
+  // warp publishes each item's live query tiles (a bit per 128-row tile whose
+  // mask block with the key tile has a set bit) kSlots items ahead; the other
+  // warps walk only those.  Counters over all items of the CTA: j (items; list
+  // slot j % kSlots), li (items with a live tile; K/V buffer li % kKVBufs), lt
+  // (live query tiles; staging buffer lt % kQBufs).
   const int G = static_cast<int>(gridDim.x);
   const int n_items = (total_items - static_cast<int>(blockIdx.x) + G - 1) / G;
   volatile uint32_t* abort_flag = &ctl.abort_flag;
@@ -250,8 +273,11 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
       mbar_init(smem_u32(&ctl.kv_full[b]), 1);
       mbar_init(smem_u32(&ctl.kv_free[b]), 1);
       mbar_init(smem_u32(&ctl.ld_full[b]), 1);
-      mbar_init(smem_u32(&ctl.tile_free[b]), C::kEwWarps + 5);  // compute + 4 epilogue warps + the MMA issuer
-      ctl.live[b] = 0;
+      mbar_init(smem_u32(&ctl.tile_free[b]), C::kEwWarps + 1);  // compute warps + the MMA issuer
+    }
+    for (int sl = 0; sl < kSlots; ++sl) {
+      mbar_init(smem_u32(&ctl.item_full[sl]), 1);
+      mbar_init(smem_u32(&ctl.item_free[sl]), C::kEwWarps + 6);  // compute, loader, MMA, 4 epilogue warps
     }
     mbar_init(smem_u32(&ctl.acc_free), 4);
     mbar_init(smem_u32(&ctl.st_full), 1);
@@ -278,6 +304,11 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
     ctl.abort_flag = 1;
     atomicOr(err_word, kDevErrTimeout);
   };
+  // Whole-warp wait on the live list of item j.
+  auto wait_item = [&](int j) -> bool {
+    return __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&ctl.item_full[j % kSlots]), (j / kSlots) & 1,
+                                                      abort_flag, timeout_ns));
+  };
 
   if (warp == C::kLoaderWarp) {
     // ================================================================ loader
@@ -289,22 +320,15 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
       tma_prefetch_desc(&tm_dq);
     }
     bool ok = true;
-    int gq = 0;
-    int last_copy = -1;  // last query tile (in gq) whose Q/dO copies were started
-    int kv_copies = 0;   // items whose K/V copies were started
-    const int n_tiles = n_items * QT;
-    // Mask words, LSE and Delta of query tile g (4 rows per lane): all loads
-    // issued at once, into registers.
-    auto fetch = [&](int g, uint32_t (&w4)[4][4], float (&l2)[4], float (&de)[4]) {
-      const int jj = g / QT;
-      const int item = static_cast<int>(blockIdx.x) + jj * G;
-      const int fbh = item / KT;
-      const int fkt = item - fbh * KT;
-      const int i0 = (g - jj * QT) * kT;
+    int lt = 0, li = 0;  // li: live items, whose K/V copies were started
+    int last_copy = -1;  // last live tile (in lt) whose Q/dO copies were started
+    // Mask words, LSE and Delta of query tile qt of (bh, kt), 4 rows per lane:
+    // all loads issued at once, into registers.
+    auto fetch = [&](int fbh, int fkt, int qt, uint32_t (&w4)[4][4], float (&l2)[4], float (&de)[4]) {
 #pragma unroll
       for (int rr = 0; rr < 4; ++rr) {
-        const int row = i0 + lane + 32 * rr;
-        const bool in = row < N;
+        const int row = qt * kT + lane + 32 * rr;
+        const bool in = qt >= 0 && row < N;
         const int64_t r64 = static_cast<int64_t>(fbh) * N + (in ? row : 0);
         const uint32_t* mrow = mask + r64 * W + fkt * 4;
         if (vec) {
@@ -322,23 +346,14 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
         de[rr] = in ? __ldg(delta + r64) : 0.f;
       }
     };
-    // The loads of tile g+1 are issued before tile g waits for its buffer, so
-    // their latency overlaps a whole tile instead of delaying the staging.
-    uint32_t nw[4][4];
-    float nl[4], nd[4];
-    fetch(0, nw, nl, nd);
-    for (int j = 0; ok && j < n_items; ++j) {
-      const int item = static_cast<int>(blockIdx.x) + j * G;
-      const int bh = item / KT;
-      const int kt = item - bh * KT;
-      const int bkv = j % kKVBufs;
-      // K/V buffer bkv is free once the MMAs of item j - kKVBufs are complete.
-      if (j >= kKVBufs &&
-          !__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&ctl.kv_free[bkv]), ((j - kKVBufs) / kKVBufs) & 1,
-                                                     abort_flag, timeout_ns))) {
-        ok = false;
-        break;
-      }
+    // K and V of the next live item into buffer li % kKVBufs, once the
+    // products of live item li - kKVBufs are complete.
+    auto issue_kv = [&](int bh, int kt) -> bool {
+      const int bkv = li % kKVBufs;
+      if (li >= kKVBufs &&
+          !__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&ctl.kv_free[bkv]), ((li - kKVBufs) / kKVBufs) & 1,
+                                                     abort_flag, timeout_ns)))
+        return false;
       if (lane == 0) {
         mbar_arrive_expect_tx(smem_u32(&ctl.kv_full[bkv]), 2 * kTileBytes);
 #pragma unroll
@@ -349,82 +364,146 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
                       dc * 64, kt * kT, bh);
         }
       }
-      ++kv_copies;
-      for (int qi = 0; qi < QT; ++qi, ++gq) {
-        const int b = gq % kQBufs;
-        uint32_t w4[4][4];
-        float l2[4], de[4];
+      ++li;
+      return true;
+    };
+    // Live tile lt (query tile qt of (bh, kt)) into staging buffer lt % kQBufs,
+    // once the compute warps are done with live tile lt - kQBufs and the
+    // products reading its Q / dO are complete (the MMA issuer's arrival is a
+    // tcgen05.commit).
+    auto stage = [&](int bh, int kt, int qt, const uint32_t (&w4)[4][4], const float (&l2)[4],
+                     const float (&de)[4]) -> bool {
+      const int b = lt % kQBufs;
+      if (lt >= kQBufs &&
+          !__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&ctl.tile_free[b]), ((lt - kQBufs) / kQBufs) & 1,
+                                                     abort_flag, timeout_ns)))
+        return false;
 #pragma unroll
-        for (int rr = 0; rr < 4; ++rr) {
-          l2[rr] = nl[rr];
-          de[rr] = nd[rr];
+      for (int rr = 0; rr < 4; ++rr) {
+        const int i = lane + 32 * rr;
 #pragma unroll
-          for (int w = 0; w < 4; ++w) w4[rr][w] = nw[rr][w];
+        for (int w = 0; w < 4; ++w) s_mask[b * 4 * kT + w * kT + i] = w4[rr][w] & valid_bits(kt * 4 + w, N);
+        // -FLT_MAX (a row with no kept key) becomes -inf; such a row has no
+        // mask bit, so its P is 0 by the select and never uses this value.
+        s_lse[b * kT + i] = l2[rr] * kLog2e;
+        s_delta[b * kT + i] = de[rr];
+      }
+      __syncwarp();
+      if (lane == 0) {
+        mbar_arrive_expect_tx(smem_u32(&ctl.ld_full[b]), 2 * kTileBytes);
+#pragma unroll
+        for (int dc = 0; dc < C::kDChunks; ++dc) {
+          tma_load_3d(base + C::kOffQ + b * kTileBytes + dc * kT * 128, &tm_q, smem_u32(&ctl.ld_full[b]), dc * 64,
+                      qt * kT, bh);
+          tma_load_3d(base + C::kOffDO + b * kTileBytes + dc * kT * 128, &tm_do, smem_u32(&ctl.ld_full[b]),
+                      dc * 64, qt * kT, bh);
         }
-        if (gq + 1 < n_tiles) fetch(gq + 1, nw, nl, nd);
-        // Buffer b is free once the compute and epilogue warps are done with
-        // tile gq - kQBufs and the products reading its Q / dO are complete
-        // (the MMA issuer's arrival is a tcgen05.commit for a live tile).
-        if (gq >= kQBufs &&
-            !__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&ctl.tile_free[b]), ((gq - kQBufs) / kQBufs) & 1,
-                                                       abort_flag, timeout_ns))) {
+        last_copy = lt;
+      }
+      ++lt;
+      return true;
+    };
+    // Start-up: the scanner always lists query tile 0 of item 0 (a tile with
+    // no kept key adds zeros), so item 0's K/V and that tile are loaded and
+    // staged here, while its list is being scanned.
+    {
+      const int bh0 = static_cast<int>(blockIdx.x) / KT;
+      const int kt0 = static_cast<int>(blockIdx.x) - bh0 * KT;
+      uint32_t w4[4][4];
+      float l2[4], de[4];
+      fetch(bh0, kt0, 0, w4, l2, de);
+      ok = issue_kv(bh0, kt0) && stage(bh0, kt0, 0, w4, l2, de);
+    }
+    // The loads of the next live tile are issued before this one waits for
+    // its buffer, so their latency overlaps a tile; at an item's last live
+    // tile that is the first live tile of the next item, when it has one.
+    uint32_t nw[4][4];
+    float nl[4], nd[4];
+    bool have_next = false;  // nw / nl / nd hold the first live tile of item j
+    for (int j = 0; ok && j < n_items; ++j) {
+      if (!wait_item(j)) {
+        ok = false;
+        break;
+      }
+      const int sl = j % kSlots;
+      const int n = static_cast<int>(ctl.n_live[sl]);
+      if (n > 0) {
+        const int item = static_cast<int>(blockIdx.x) + j * G;
+        const int bh = item / KT;
+        const int kt = item - bh * KT;
+        if (j > 0 && !issue_kv(bh, kt)) {
           ok = false;
           break;
         }
-        const int i0 = qi * kT;
-        uint32_t any = 0u;
-#pragma unroll
-        for (int rr = 0; rr < 4; ++rr) {
-          const int i = lane + 32 * rr;
-#pragma unroll
-          for (int w = 0; w < 4; ++w) {
-            const uint32_t x = w4[rr][w] & valid_bits(kt * 4 + w, N);
-            s_mask[b * 4 * kT + w * kT + i] = x;
-            any |= x;
-          }
-          // -FLT_MAX (a row with no kept key) becomes -inf; such a row has no
-          // mask bit, so its P is 0 by the select and never uses this value.
-          s_lse[b * kT + i] = l2[rr] * kLog2e;
-          s_delta[b * kT + i] = de[rr];
+        const uint32_t* bits = ctl.live_bits[sl];
+        int cw = 0;
+        uint32_t cx = bits[0];
+        int qt_next = next_live_tile(bits, cw, cx);
+        int t0 = 0;
+        if (j == 0) {  // its tile 0 (always listed, the lowest bit) is staged
+          qt_next = next_live_tile(bits, cw, cx);
+          t0 = 1;
         }
-        const bool live = __any_sync(0xffffffffu, any != 0u);
-        __syncwarp();
-        if (lane == 0) {
-          ctl.live[b] = live ? 1u : 0u;
-          if (live) {
-            mbar_arrive_expect_tx(smem_u32(&ctl.ld_full[b]), 2 * kTileBytes);
+        if (t0 < n && !have_next) fetch(bh, kt, qt_next, nw, nl, nd);
+        have_next = false;
+        for (int t = t0; t < n; ++t) {
+          const int qt = qt_next;
+          uint32_t w4[4][4];
+          float l2[4], de[4];
 #pragma unroll
-            for (int dc = 0; dc < C::kDChunks; ++dc) {
-              tma_load_3d(base + C::kOffQ + b * kTileBytes + dc * kT * 128, &tm_q, smem_u32(&ctl.ld_full[b]),
-                          dc * 64, i0, bh);
-              tma_load_3d(base + C::kOffDO + b * kTileBytes + dc * kT * 128, &tm_do, smem_u32(&ctl.ld_full[b]),
-                          dc * 64, i0, bh);
+          for (int rr = 0; rr < 4; ++rr) {
+            l2[rr] = nl[rr];
+            de[rr] = nd[rr];
+#pragma unroll
+            for (int w = 0; w < 4; ++w) w4[rr][w] = nw[rr][w];
+          }
+          if (t + 1 < n) {
+            qt_next = next_live_tile(bits, cw, cx);
+            fetch(bh, kt, qt_next, nw, nl, nd);
+          } else if (j + 1 < n_items) {
+            // The next item's list (published kSlots items ahead of the
+            // slowest reader, so never behind this warp's own release).
+            if (!wait_item(j + 1)) {
+              ok = false;
+              break;
             }
-            last_copy = gq;
-          } else {
-            mbar_arrive(smem_u32(&ctl.ld_full[b]));
+            const int sl1 = (j + 1) % kSlots;
+            if (ctl.n_live[sl1] > 0u) {
+              int w1 = 0;
+              uint32_t x1 = ctl.live_bits[sl1][0];
+              const int item1 = item + G;
+              fetch(item1 / KT, item1 - (item1 / KT) * KT, next_live_tile(ctl.live_bits[sl1], w1, x1), nw, nl, nd);
+              have_next = true;
+            }
+          }
+          if (!stage(bh, kt, qt, w4, l2, de)) {
+            ok = false;
+            break;
           }
         }
+        if (!ok) break;
       }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&ctl.item_free[sl]));
     }
     if (!ok && lane == 0) {
       fail();
       // Let the copies this warp started land before the CTA exits.
       uint32_t zero = 0;
-      for (int jj = kv_copies - kKVBufs; jj < kv_copies; ++jj)
+      for (int jj = li - kKVBufs; jj < li; ++jj)
         if (jj >= 0) mbar_wait_bounded(smem_u32(&ctl.kv_full[jj % kKVBufs]), (jj / kKVBufs) & 1, &zero, timeout_ns);
       for (int g = last_copy - kQBufs + 1; g <= last_copy; ++g)
         if (g >= 0) mbar_wait_bounded(smem_u32(&ctl.ld_full[g % kQBufs]), (g / kQBufs) & 1, &zero, timeout_ns);
     }
   } else if (warp == C::kMmaWarp) {
     // ================================================================ MMA issuer
+    bool ok = true;
     if (lane == 0) {
       constexpr uint32_t idesc_s = make_idesc_f16(kT, kT, BF16 ? 1 : 0, 0);       // S^T, dP^T (M = keys)
       constexpr uint32_t idesc_kv = make_idesc_f16(kT, D, BF16 ? 1 : 0, 1);       // dV, dK (B M/N-major)
       constexpr uint32_t idesc_q = make_idesc_f16(kT, 64, BF16 ? 1 : 0, 1, 1);    // dQ half (A and B M/N-major)
-      bool ok = true;
-      int gq = 0;
       uint32_t lt = 0;
+      int li = 0;
       // dQ_part = dS K of live tile L (K of its item at sKL) in 64-dim halves:
       // 16 keys per step; dS's two 64-query chunks are kT * 128 bytes apart,
       // as are K's 64-dim chunks.  With dQ_part in its own columns, the
@@ -445,9 +524,8 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
         return true;
       };
       // D = 64: the live tile whose dQ_part is still to be issued, the K it
-      // reads, its item, and (once that item has ended) the K/V buffer to
-      // release after it.
-      int pend = -1, pend_item = -1, pend_kv = -1;
+      // reads, and (once its item has ended) the K/V buffer to release after it.
+      int pend = -1, pend_kv = -1;
       uint32_t pend_sk = 0;
       auto flush = [&]() -> bool {
         if (pend < 0) return true;
@@ -458,127 +536,185 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
         return true;
       };
       for (int j = 0; ok && j < n_items; ++j) {
-        const int bkv = j % kKVBufs;
-        const uint32_t sK = base + C::kOffK + bkv * kTileBytes, sV = base + C::kOffV + bkv * kTileBytes;
-        if (!mbar_wait_bounded(smem_u32(&ctl.kv_full[bkv]), (j / kKVBufs) & 1, abort_flag, timeout_ns)) {
+        const int sl = j % kSlots;
+        if (!mbar_wait_bounded(smem_u32(&ctl.item_full[sl]), (j / kSlots) & 1, abort_flag, timeout_ns)) {
           ok = false;
           break;
         }
-        uint32_t item_lt = 0;  // live query tiles of this item so far
-        for (int qi = 0; qi < QT; ++qi, ++gq) {
-          const int b = gq % kQBufs;
-          const uint32_t sQ = base + C::kOffQ + b * kTileBytes, sDO = base + C::kOffDO + b * kTileBytes;
-          if (!mbar_wait_bounded(smem_u32(&ctl.ld_full[b]), (gq / kQBufs) & 1, abort_flag, timeout_ns)) {
+        const int n = static_cast<int>(ctl.n_live[sl]);
+        if (n > 0) {
+          const int bkv = li % kKVBufs;
+          const uint32_t sK = base + C::kOffK + bkv * kTileBytes, sV = base + C::kOffV + bkv * kTileBytes;
+          if (!mbar_wait_bounded(smem_u32(&ctl.kv_full[bkv]), (li / kKVBufs) & 1, abort_flag, timeout_ns)) {
             ok = false;
             break;
           }
-          if (ctl.live[b] == 0u) {
-            // D = 64: a pending dQ_part is issued in the slot of the very next
-            // tile, live or not.  (The epilogue warps wait for it before they
-            // release later staging buffers, so it may not wait for a later
-            // live tile.)
+          for (int t = 0; t < n; ++t, ++lt) {
+            const int b = lt % kQBufs;
+            const uint32_t sQ = base + C::kOffQ + b * kTileBytes, sDO = base + C::kOffDO + b * kTileBytes;
+            // Tile lt staged.  The S^T / dP^T columns are free once the
+            // previous live tile's dV / dK products (which read P^T / dS^T
+            // there) are complete and, where dQ_part shares those columns
+            // (D = 128), its dQ_part has been read.  MMAs into different
+            // accumulators are not ordered by issue.
+            if (!mbar_wait_bounded(smem_u32(&ctl.ld_full[b]), (lt / kQBufs) & 1, abort_flag, timeout_ns) ||
+                (lt > 0 && !mbar_wait_bounded(smem_u32(C::kDQApart ? &ctl.pt_free : &ctl.dq_free), (lt - 1) & 1,
+                                              abort_flag, timeout_ns))) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            // 16 head dims per step: swizzle chunk kk/4 of the rows, 32 bytes into it.
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t off = (kk >> 2) * (kT * 128) + (kk & 3) * 32;
+              mma_ss(tmem + kColS, smem_desc_sw128(sK + off, 16, 1024), smem_desc_sw128(sQ + off, 16, 1024), idesc_s,
+                     kk > 0 ? 1u : 0u);
+            }
+#pragma unroll
+            for (int kk = 0; kk < D / 16; ++kk) {
+              const uint32_t off = (kk >> 2) * (kT * 128) + (kk & 3) * 32;
+              mma_ss(tmem + kColDP, smem_desc_sw128(sV + off, 16, 1024), smem_desc_sw128(sDO + off, 16, 1024),
+                     idesc_s, kk > 0 ? 1u : 0u);
+            }
+            // st_full also covers every earlier product, so the dQ_part that
+            // last read this tile's dS buffer has done so before it is rewritten.
+            mma_commit(smem_u32(&ctl.st_full));
+            // D = 64: the previous live tile's dQ_part, behind this tile's S^T / dP^T.
             if (C::kDQApart && !flush()) {
               ok = false;
               break;
             }
-            mbar_arrive(smem_u32(&ctl.tile_free[b]));
-            continue;
-          }
-          // The S^T / dP^T columns are free once the previous live tile's dV /
-          // dK products (which read P^T / dS^T there) are complete and, where
-          // dQ_part shares those columns (D = 128), its dQ_part has been read.
-          // MMAs into different accumulators are not ordered by issue.
-          if (lt > 0 && !mbar_wait_bounded(smem_u32(C::kDQApart ? &ctl.pt_free : &ctl.dq_free), (lt - 1) & 1,
-                                           abort_flag, timeout_ns)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          // 16 head dims per step: swizzle chunk kk/4 of the rows, 32 bytes into it.
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * (kT * 128) + (kk & 3) * 32;
-            mma_ss(tmem + kColS, smem_desc_sw128(sK + off, 16, 1024), smem_desc_sw128(sQ + off, 16, 1024), idesc_s,
-                   kk > 0 ? 1u : 0u);
-          }
-#pragma unroll
-          for (int kk = 0; kk < D / 16; ++kk) {
-            const uint32_t off = (kk >> 2) * (kT * 128) + (kk & 3) * 32;
-            mma_ss(tmem + kColDP, smem_desc_sw128(sV + off, 16, 1024), smem_desc_sw128(sDO + off, 16, 1024), idesc_s,
-                   kk > 0 ? 1u : 0u);
-          }
-          // st_full also covers every earlier product, so the dQ_part that
-          // last read this tile's dS buffer has done so before it is rewritten.
-          mma_commit(smem_u32(&ctl.st_full));
-          // D = 64: the previous live tile's dQ_part, behind this tile's S^T / dP^T.
-          if (C::kDQApart && !flush()) {
-            ok = false;
-            break;
-          }
-          // P^T / dS^T of this tile; before the first dV / dK product of item
-          // j, the epilogue warps must have read item j-1's dV / dK.
-          if (!mbar_wait_bounded(smem_u32(&ctl.p_full), lt & 1, abort_flag, timeout_ns) ||
-              (item_lt == 0 && j > 0 &&
-               !mbar_wait_bounded(smem_u32(&ctl.acc_free), (j - 1) & 1, abort_flag, timeout_ns))) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          // 16 query rows per step: 8 packed TMEM columns of P^T / dS^T, 2048
-          // bytes (16 rows of 128) into the M/N-major shared-memory operands,
-          // whose 64-dim chunks (D = 128) are kT * 128 bytes apart.
-#pragma unroll
-          for (int kk = 0; kk < kT / 16; ++kk)
-            mma_ts(tmem + kColDV, tmem + C::col_p(kk >> 1) + (kk & 1) * 8, smem_desc_sw128(sDO + kk * 2048, kT * 128, 1024),
-                   idesc_kv, (item_lt > 0 || kk > 0) ? 1u : 0u);
-#pragma unroll
-          for (int kk = 0; kk < kT / 16; ++kk)
-            mma_ts(tmem + C::kColDK, tmem + C::col_ds(kk >> 1) + (kk & 1) * 8,
-                   smem_desc_sw128(sQ + kk * 2048, kT * 128, 1024), idesc_kv, (item_lt > 0 || kk > 0) ? 1u : 0u);
-          if constexpr (C::kDQApart) {
-            mma_commit(smem_u32(&ctl.pt_free));
-            // Q / dO of the staging buffer are released when dV / dK complete.
-            mma_commit(smem_u32(&ctl.tile_free[b]));
-            pend = static_cast<int>(lt);
-            pend_item = j;
-            pend_sk = sK;
-          } else {
-            // Q / dO of the staging buffer are released when dV / dK complete
-            // (the dQ product reads neither), so the next tile's loads start
-            // while it runs.
-            mma_commit(smem_u32(&ctl.tile_free[b]));
-            if (!issue_dq(lt, sK)) {
+            // P^T / dS^T of this tile; before the first dV / dK product of a
+            // live item, the epilogue warps must have read the previous live
+            // item's dV / dK.
+            if (!mbar_wait_bounded(smem_u32(&ctl.p_full), lt & 1, abort_flag, timeout_ns) ||
+                (t == 0 && li > 0 && !mbar_wait_bounded(smem_u32(&ctl.acc_free), (li - 1) & 1, abort_flag, timeout_ns))) {
               ok = false;
               break;
             }
+            tc_fence_after();
+            // 16 query rows per step: 8 packed TMEM columns of P^T / dS^T, 2048
+            // bytes (16 rows of 128) into the M/N-major shared-memory operands,
+            // whose 64-dim chunks (D = 128) are kT * 128 bytes apart.
+#pragma unroll
+            for (int kk = 0; kk < kT / 16; ++kk)
+              mma_ts(tmem + kColDV, tmem + C::col_p(kk >> 1) + (kk & 1) * 8,
+                     smem_desc_sw128(sDO + kk * 2048, kT * 128, 1024), idesc_kv, (t > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+            for (int kk = 0; kk < kT / 16; ++kk)
+              mma_ts(tmem + C::kColDK, tmem + C::col_ds(kk >> 1) + (kk & 1) * 8,
+                     smem_desc_sw128(sQ + kk * 2048, kT * 128, 1024), idesc_kv, (t > 0 || kk > 0) ? 1u : 0u);
+            // Q / dO of the staging buffer are released when dV / dK complete
+            // (the dQ product reads neither).
+            if constexpr (C::kDQApart) {
+              mma_commit(smem_u32(&ctl.pt_free));
+              mma_commit(smem_u32(&ctl.tile_free[b]));
+              pend = static_cast<int>(lt);
+              pend_sk = sK;
+            } else {
+              mma_commit(smem_u32(&ctl.tile_free[b]));
+              if (!issue_dq(lt, sK)) {
+                ok = false;
+                break;
+              }
+            }
           }
-          ++lt;
-          ++item_lt;
-        }
-        if (!ok) break;
-        // K/V buffer bkv may be refilled once this item's products are
-        // complete.  D = 64: a dQ_part pending from this item (its last tile
-        // was live) releases bkv when it is issued, in the next tile's slot.
-        if constexpr (C::kDQApart) {
-          if (pend >= 0 && pend_item < j && !flush()) {
-            ok = false;
-            break;
-          }
-          if (pend >= 0)
+          if (!ok) break;
+          ++li;
+          // K/V buffer bkv may be refilled once this item's products are
+          // complete.  D = 64: the last tile's dQ_part stays pending (issued
+          // behind the next tile's S^T / dP^T, and bkv released after it) only
+          // when the next item has a live tile; otherwise it is issued now, so
+          // no warp waits on it across items the scanner has yet to publish.
+          if constexpr (C::kDQApart) {
+            bool keep = false;
+            if (j + 1 < n_items) {
+              if (!mbar_wait_bounded(smem_u32(&ctl.item_full[(j + 1) % kSlots]), ((j + 1) / kSlots) & 1, abort_flag,
+                                     timeout_ns)) {
+                ok = false;
+                break;
+              }
+              keep = ctl.n_live[(j + 1) % kSlots] > 0u;
+            }
             pend_kv = bkv;
-          else
+            if (!keep && !flush()) {
+              ok = false;
+              break;
+            }
+          } else {
             mma_commit(smem_u32(&ctl.kv_free[bkv]));
-        } else {
-          mma_commit(smem_u32(&ctl.kv_free[bkv]));
+          }
         }
+        mbar_arrive(smem_u32(&ctl.item_free[sl]));
       }
-      if (ok && C::kDQApart && !flush()) ok = false;
+      if (ok && !flush()) ok = false;
       if (!ok) fail();
       // Every MMA this thread issued must complete before TMEM is released.
       mma_commit(smem_u32(&ctl.drain));
       uint32_t zero = 0;
       mbar_wait_bounded(smem_u32(&ctl.drain), 0, &zero, timeout_ns);
     }
+  } else if (warp == C::kScanWarp) {
+    // ================================================================ scanner
+    // Item j's live list: bit qt set when some query row of tile qt keeps a
+    // key of the item's key tile.  4 query tiles per batch, 4 rows per lane.
+    bool ok = true;
+    for (int j = 0; j < n_items; ++j) {
+      const int sl = j % kSlots;
+      if (j >= kSlots &&
+          !__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&ctl.item_free[sl]), ((j / kSlots) - 1) & 1,
+                                                     abort_flag, timeout_ns))) {
+        ok = false;
+        break;
+      }
+      const int item = static_cast<int>(blockIdx.x) + j * G;
+      const int bh = item / KT;
+      const int kt = item - bh * KT;
+      uint32_t vmask[4];
+#pragma unroll
+      for (int w = 0; w < 4; ++w) vmask[w] = valid_bits(kt * 4 + w, N);
+      uint32_t my_word = 0u;  // lane w: word w of the list
+      for (int q0 = 0; q0 < QT; q0 += 4) {
+        uint4 v[4][4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+#pragma unroll
+          for (int rr = 0; rr < 4; ++rr) {
+            const int row = (q0 + u) * kT + lane + 32 * rr;
+            uint4 x = make_uint4(0u, 0u, 0u, 0u);
+            if (q0 + u < QT && row < N) {
+              const uint32_t* mrow = mask + (static_cast<int64_t>(bh) * N + row) * W + kt * 4;
+              if (vec) {
+                x = __ldg(reinterpret_cast<const uint4*>(mrow));
+              } else {
+                x.x = __ldg(mrow);
+                x.y = kt * 4 + 1 < W ? __ldg(mrow + 1) : 0u;
+                x.z = kt * 4 + 2 < W ? __ldg(mrow + 2) : 0u;
+                x.w = kt * 4 + 3 < W ? __ldg(mrow + 3) : 0u;
+              }
+            }
+            v[u][rr] = x;
+          }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          uint32_t any = 0u;
+#pragma unroll
+          for (int rr = 0; rr < 4; ++rr)
+            any |= (v[u][rr].x & vmask[0]) | (v[u][rr].y & vmask[1]) | (v[u][rr].z & vmask[2]) |
+                   (v[u][rr].w & vmask[3]);
+          const int qt = q0 + u;
+          if (__any_sync(0xffffffffu, any != 0u) && lane == (qt >> 5)) my_word |= 1u << (qt & 31);
+        }
+      }
+      if (j == 0 && lane == 0) my_word |= 1u;  // item 0's tile 0 is staged at start-up, listed or not
+      if (lane < kLiveWords) ctl.live_bits[sl][lane] = my_word;
+      const int n = __reduce_add_sync(0xffffffffu, __popc(my_word));
+      if (lane == 0) ctl.n_live[sl] = static_cast<uint32_t>(n);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&ctl.item_full[sl]));
+    }
+    if (!ok && lane == 0) fail();
   } else {
     auto wait_all = [&](uint64_t& bar, uint32_t parity) -> bool {
       const bool all =
@@ -596,23 +732,23 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
     const int t = (warp & 3) * 32 + lane;
     const uint32_t t_lane = tmem + (static_cast<uint32_t>((warp & 3) * 32) << 16);
     bool ok = true;
-    int gq = 0;
     uint32_t lt = 0;
     if (warp < C::kEwWarps) {
       // ============================================================== compute
       const float c2 = scale * kLog2e;
       const int my_word = (t >> 5) * kT;  // the word holding this key, for each query row
       const int kb = t & 31;
-      const int n_tiles = n_items * QT;
-      for (; gq < n_tiles; ++gq) {
-        const int b = gq % kQBufs;
-        const uint32_t* my_words = s_mask + b * 4 * kT + my_word;
-        const float* t_lse = s_lse + b * kT;
-        const float* t_delta = s_delta + b * kT;
-        ok = wait_all(ctl.ld_full[b], (gq / kQBufs) & 1);
+      for (int j = 0; ok && j < n_items; ++j) {
+        ok = wait_all(ctl.item_full[j % kSlots], (j / kSlots) & 1);
         if (!ok) break;
-        if (ctl.live[b] != 0u) {
-          ok = wait_all(ctl.st_full, lt & 1);
+        const int n = static_cast<int>(ctl.n_live[j % kSlots]);
+        arrive_warp(ctl.item_free[j % kSlots]);  // only the count is needed
+        for (int tt = 0; tt < n; ++tt, ++lt) {
+          const int b = lt % kQBufs;
+          const uint32_t* my_words = s_mask + b * 4 * kT + my_word;
+          const float* t_lse = s_lse + b * kT;
+          const float* t_delta = s_delta + b * kT;
+          ok = wait_all(ctl.ld_full[b], (lt / kQBufs) & 1) && wait_all(ctl.st_full, lt & 1);
           if (!ok) break;
 #pragma unroll 1
           for (int c = (warp >> 2) * C::kChunksPerWarp; c < ((warp >> 2) + 1) * C::kChunksPerWarp; ++c) {
@@ -656,28 +792,29 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
           tmem_wait_st();
           fence_proxy_async_smem();  // dS written by this thread, read by the tensor core
           arrive_warp(ctl.p_full);
-          ++lt;
+          arrive_warp(ctl.tile_free[b]);
         }
-        arrive_warp(ctl.tile_free[b]);
       }
     } else {
       // ============================================================== epilogue
       uint8_t* s_dq = smem + C::kOffDQ + (warp & 3) * (C::kStageBoxes * 4096);
+      uint32_t li = 0;
       for (int j = 0; ok && j < n_items; ++j) {
+        const int sl = j % kSlots;
+        ok = wait_all(ctl.item_full[sl], (j / kSlots) & 1);
+        if (!ok) break;
         const int item = static_cast<int>(blockIdx.x) + j * G;
         const int bh = item / KT;
         const int key = (item - bh * KT) * kT + t;
-        uint32_t item_lt = 0;
-        for (int qi = 0; qi < QT; ++qi, ++gq) {
-          const int b = gq % kQBufs;
-          ok = wait_all(ctl.ld_full[b], (gq / kQBufs) & 1);
-          if (!ok) break;
-          const bool live = ctl.live[b] != 0u;
-          arrive_warp(ctl.tile_free[b]);  // only live[b] is read from the buffer
-          if (!live) continue;
+        const int n = static_cast<int>(ctl.n_live[sl]);
+        const uint32_t* bits = ctl.live_bits[sl];
+        int cw = 0;
+        uint32_t cx = bits[0];
+        for (int tt = 0; tt < n; ++tt, ++lt) {
+          const int qt = next_live_tile(bits, cw, cx);
           ok = wait_all(ctl.dq_full, lt & 1);
           if (!ok) break;
-          // dQ_part row t = query row qi*128 + t: all of it into registers,
+          // dQ_part row t = query row qt*128 + t: all of it into registers,
           // TMEM released, then scaled, staged (this warp's 32 rows) and added
           // into the FP32 accumulator by TMA bulk reduce-adds, kStageBoxes
           // boxes of 32 columns per pass.  A box starting at or past row N has
@@ -687,7 +824,7 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
           for (int h = 0; h < D / 32; ++h) tmem_ld32f(t_lane + C::col_dq(h >> 1) + (h & 1) * 32, u + 32 * h);
           tmem_wait_ld();
           arrive_warp(ctl.dq_free);
-          const int row0 = qi * kT + (warp & 3) * 32;
+          const int row0 = qt * kT + (warp & 3) * 32;
 #pragma unroll
           for (int pass = 0; pass < D / (32 * C::kStageBoxes); ++pass) {
             // This warp's staging area is free once its previous reduce-adds have read it.
@@ -705,15 +842,13 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
             }
             fence_proxy_async_smem();  // staged by every lane, read by the TMA unit
             __syncwarp();
-            if (lane == 0 && row0 < N) {
+            if (lane == 0 && qt >= 0 && row0 < N) {
 #pragma unroll
               for (int h = 0; h < C::kStageBoxes; ++h)
                 tma_reduce_add_3d(&tm_dq, smem_u32(s_dq + h * 4096), (C::kStageBoxes * pass + h) * 32, row0, bh);
               bulk_commit_group();
             }
           }
-          ++lt;
-          ++item_lt;
         }
         if (!ok) break;
         // dV and dK of this key tile (lane t = key); zero when no query tile
@@ -722,7 +857,7 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
 #pragma unroll 1
         for (int h = 0; h < D / 32; ++h) {
           uint32_t vw[16], kw[16];
-          if (item_lt > 0) {
+          if (n > 0) {
             float u[32];
             tmem_ld32f(t_lane + kColDV + h * 32, u);
             tmem_wait_ld();
@@ -746,7 +881,11 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
             }
           }
         }
-        arrive_warp(ctl.acc_free);
+        if (n > 0) {
+          arrive_warp(ctl.acc_free);  // live item li's dV / dK read out of TMEM
+          ++li;
+        }
+        arrive_warp(ctl.item_free[sl]);
       }
       // The reduce-adds must finish (and stop reading shared memory) before the CTA exits.
       if (lane == 0) bulk_wait_group0();
