@@ -16,8 +16,9 @@
 //   attn_bwd_kernel    persistent, one CTA per SM looping over the items
 //                      (batch*head, 128-key tile).  Per item K and V stay in
 //                      shared memory, dK and dV accumulate in TMEM, and the
-//                      CTA walks the 128-row query tiles whose mask block with
-//                      its key tile has a set bit.  Per live query tile:
+//                      CTA walks only the 128-row query tiles whose mask block
+//                      with its key tile has a set bit (listed ahead by a
+//                      scanner warp).  Per live query tile:
 //                        MMA  S^T = K Q^T, dP^T = V dO^T   (M = keys)
 //                        P^T, dS^T in registers (thread t = key t), written
 //                        back to TMEM (fp16/bf16) and dS to shared memory
@@ -34,7 +35,8 @@
 // Delta of the query tile staged in shared memory), E+1 MMA issuer and TMEM
 // owner, E+2..E+5 epilogue (dQ_part of each live tile into the FP32
 // accumulator, dK and dV of each item; warp w reads TMEM lanes 32(w%4)..+31),
-// so the epilogues of one tile overlap the element-wise work of the next.
+// so the epilogues of one tile overlap the element-wise work of the next, E+6
+// scanner (each item's live query tiles, kSlots items ahead).
 // TMEM layout per head dim: see BwdCfg.
 // Every wait is bounded and reports through the device error word.
 #include <cfloat>
