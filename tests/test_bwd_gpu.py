@@ -132,3 +132,23 @@ def test_long_sequence_backward():
     want = oracle.attention_backward(*(x.float().cpu().numpy() for x in (q, k, v)), m.cpu().numpy(),
                                      1 / 8.0, dout.float().cpu().numpy())
     check_grads((dq, dk, dv), want, torch.float16, m.cpu())
+
+
+@pytest.mark.parametrize("N,D,dtype", [(5000, 64, torch.float16), (8320, 128, torch.bfloat16)])
+def test_long_banded_backward(N, D, dtype):
+    """Long rows whose 128x128 tiles are mostly dead: a band around the
+    diagonal plus scattered 256x256 blocks, so each key tile's list of live
+    query tiles spans several 32-tile words with gaps.  Checked against the
+    oracle."""
+    g = torch.Generator(device=DEV).manual_seed(23)
+    q, k, v, dout = (torch.randn(1, 1, N, D, generator=g, device=DEV).to(dtype) for _ in range(4))
+    i = torch.arange(N, device=DEV)
+    band = (i[:, None] - i[None, :]).abs() < 300
+    nb = (N + 255) // 256
+    blocks = torch.rand(nb, nb, generator=g, device=DEV) < 0.04
+    blocks = blocks.repeat_interleave(256, 0).repeat_interleave(256, 1)[:N, :N]
+    m = (band | (blocks & (torch.rand(N, N, generator=g, device=DEV) < 0.3)))[None, None]
+    dq, dk, dv = fwd_bwd(q, k, v, m, dout)
+    want = oracle.attention_backward(*(x.float().cpu().numpy() for x in (q, k, v)), m.cpu().numpy(),
+                                     1 / math.sqrt(D), dout.float().cpu().numpy())
+    check_grads((dq, dk, dv), want, dtype, m.cpu())
