@@ -405,17 +405,6 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
       ++lt;
       return true;
     };
-    // Start-up: the scanner always lists query tile 0 of item 0 (a tile with
-    // no kept key adds zeros), so item 0's K/V and that tile are loaded and
-    // staged here, while its list is being scanned.
-    {
-      const int bh0 = static_cast<int>(blockIdx.x) / KT;
-      const int kt0 = static_cast<int>(blockIdx.x) - bh0 * KT;
-      uint32_t w4[4][4];
-      float l2[4], de[4];
-      fetch(bh0, kt0, 0, w4, l2, de);
-      ok = issue_kv(bh0, kt0) && stage(bh0, kt0, 0, w4, l2, de);
-    }
     // The loads of the next live tile are issued before this one waits for
     // its buffer, so their latency overlaps a tile; at an item's last live
     // tile that is the first live tile of the next item, when it has one.
@@ -433,7 +422,7 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
         const int item = static_cast<int>(blockIdx.x) + j * G;
         const int bh = item / KT;
         const int kt = item - bh * KT;
-        if (j > 0 && !issue_kv(bh, kt)) {
+        if (!issue_kv(bh, kt)) {
           ok = false;
           break;
         }
@@ -441,14 +430,9 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
         int cw = 0;
         uint32_t cx = bits[0];
         int qt_next = next_live_tile(bits, cw, cx);
-        int t0 = 0;
-        if (j == 0) {  // its tile 0 (always listed, the lowest bit) is staged
-          qt_next = next_live_tile(bits, cw, cx);
-          t0 = 1;
-        }
-        if (t0 < n && !have_next) fetch(bh, kt, qt_next, nw, nl, nd);
+        if (!have_next) fetch(bh, kt, qt_next, nw, nl, nd);
         have_next = false;
-        for (int t = t0; t < n; ++t) {
+        for (int t = 0; t < n; ++t) {
           const int qt = qt_next;
           uint32_t w4[4][4];
           float l2[4], de[4];
@@ -709,7 +693,6 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
           if (__any_sync(0xffffffffu, any != 0u) && lane == (qt >> 5)) my_word |= 1u << (qt & 31);
         }
       }
-      if (j == 0 && lane == 0) my_word |= 1u;  // item 0's tile 0 is staged at start-up, listed or not
       if (lane < kLiveWords) ctl.live_bits[sl][lane] = my_word;
       const int n = __reduce_add_sync(0xffffffffu, __popc(my_word));
       if (lane == 0) ctl.n_live[sl] = static_cast<uint32_t>(n);

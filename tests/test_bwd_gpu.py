@@ -152,3 +152,31 @@ def test_long_banded_backward(N, D, dtype):
     want = oracle.attention_backward(*(x.float().cpu().numpy() for x in (q, k, v)), m.cpu().numpy(),
                                      1 / math.sqrt(D), dout.float().cpu().numpy())
     check_grads((dq, dk, dv), want, dtype, m.cpu())
+
+
+@pytest.mark.parametrize("D,dtype", [(64, torch.float16), (128, torch.bfloat16)])
+def test_backward_skipped_tiles_do_not_touch_garbage(D, dtype):
+    """K / V of key tiles no row attends and Q / dO of query tiles with no kept
+    key hold NaN; the backward never reads them, so the gradients match the
+    run with clean inputs bit for bit and hold no NaN."""
+    N = 512
+    g = torch.Generator(device=DEV).manual_seed(29)
+    q, k, v, dout = (torch.randn(1, 2, N, D, generator=g, device=DEV).to(dtype) for _ in range(4))
+    m = torch.zeros(1, 2, N, N, dtype=torch.bool, device=DEV)
+    m[..., 128:384, 128:256] = torch.rand(1, 2, 256, 128, generator=g, device=DEV) < 0.3
+    clean = fwd_bwd(q, k, v, m, dout)
+    qb, kb, vb, db = (x.clone() for x in (q, k, v, dout))
+    for t in (kb, vb):
+        t[..., :128, :] = float("nan")
+        t[..., 256:, :] = float("nan")
+    for t in (qb, db):
+        t[..., :128, :] = float("nan")
+        t[..., 384:, :] = float("nan")
+    dirty = fwd_bwd(qb, kb, vb, m, db)
+    live_q = slice(128, 384)
+    live_k = slice(128, 256)
+    assert torch.equal(dirty[0][..., live_q, :], clean[0][..., live_q, :])
+    assert torch.equal(dirty[1][..., live_k, :], clean[1][..., live_k, :])
+    assert torch.equal(dirty[2][..., live_k, :], clean[2][..., live_k, :])
+    for x in dirty:
+        assert not torch.isnan(x).any()
