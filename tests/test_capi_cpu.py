@@ -113,3 +113,46 @@ def test_check_raises_with_message(lib):
     _attn(lib, dtype=9)
     with pytest.raises(L.SmaError, match="dtype"):
         L.check(L.SMA_ERR_DTYPE)
+
+
+def _bwd(lib, dtype=0, ptr=16, lse=16, mask=16, acc=16, delta=16, B=1, H=1, N=64, D=64, scale=0.125):
+    p = ptr
+    return lib.sma_attn_bwd(dtype, p, p, p, p, p, lse, mask, p, p, p, acc, delta, B, H, N, D, scale, None)
+
+
+def test_bwd_rejects_bad_arguments(lib):
+    """The backward's argument checks run before any CUDA call."""
+    assert _bwd(lib, dtype=7) == L.SMA_ERR_DTYPE
+    for d in (32, 96, 256):
+        assert _bwd(lib, D=d) == L.SMA_ERR_UNSUPPORTED_D
+    assert _bwd(lib, N=L.SMA_MAX_SEQ_LEN + 1) == L.SMA_ERR_UNSUPPORTED_N
+    assert b"65536" in lib.sma_last_error()
+    for bad in (0.0, -1.0, float("inf"), float("nan")):
+        assert _bwd(lib, scale=bad) == L.SMA_ERR_ARG
+    assert _bwd(lib, B=-1) == L.SMA_ERR_ARG
+    assert _bwd(lib, ptr=None) == L.SMA_ERR_ARG
+    assert b"null" in lib.sma_last_error()
+    assert _bwd(lib, ptr=8) == L.SMA_ERR_ARG  # q/k/v/out/dout/dq/dk/dv must be 16-byte aligned
+    assert _bwd(lib, acc=8) == L.SMA_ERR_ARG  # so must the FP32 dQ accumulator
+    assert b"16-byte" in lib.sma_last_error()
+    assert _bwd(lib, lse=2) == L.SMA_ERR_ARG  # lse / delta / mask words: 4-byte aligned
+    assert _bwd(lib, delta=6) == L.SMA_ERR_ARG
+    assert b"4-byte" in lib.sma_last_error()
+
+
+def test_bwd_empty_problem_is_a_noop(lib):
+    for dims in (dict(B=0), dict(H=0), dict(N=0)):
+        assert _bwd(lib, ptr=None, lse=None, mask=None, acc=None, delta=None, **dims) == L.SMA_OK
+
+
+def test_bwd_noalloc_rejects_problems_beyond_its_scratch(lib):
+    """B*H*N*(D+1) FP32 values must fit the fixed 32 MiB scratch; the check
+    comes before any CUDA call, and an empty problem is a no-op."""
+    def call(B, H, N, D):
+        return lib.sma_attn_bwd_noalloc(0, 16, 16, 16, 16, 16, 16, 16, 16, 16, 16, B, H, N, D, 0.125, None)
+
+    assert call(1, 256, 512, 64) == L.SMA_ERR_ARG  # 256*512*65 floats > 8 Mi
+    assert b"scratch" in lib.sma_last_error()
+    assert call(1, 1, L.SMA_MAX_SEQ_LEN + 1, 64) == L.SMA_ERR_ARG
+    assert call(-1, 1, 64, 64) == L.SMA_ERR_ARG
+    assert call(0, 1, 64, 64) == L.SMA_OK
