@@ -60,9 +60,10 @@ constexpr int kMaxDevices = 64;
 // current item computes) and the query tiles (the loader fills tile i+1 while
 // tile i is computed); D = 128 has shared memory for one of each.
 // TMEM: S^T [0,128) and dP^T [128,256) (P^T / dS^T packed over their first
-// 64 columns), dV [256, 256+D), dK [256+D, 256+2D); dQ_part in 64-column
-// halves: D = 64 at [384,448), D = 128 over the S^T / dP^T columns that
-// P^T / dS^T leave free, [64,128) and [192,256).
+// 64 columns; for D = 64 the packed P^T / dS^T of query columns 64-127 at
+// [448,480) / [480,512) instead), dV [256, 256+D), dK [256+D, 256+2D);
+// dQ_part in 64-column halves: D = 64 at [384,448), D = 128 over the S^T /
+// dP^T columns that P^T / dS^T leave free, [64,128) and [192,256).
 template <int D>
 struct BwdCfg {
   static_assert(D == 64 || D == 128, "head dim");
