@@ -132,8 +132,11 @@ SMA_API int sma_attn_bwd(int dtype, const void* q, const void* k, const void* v,
  * inside the library (one per device, found once per device with
  * cudaGetSymbolAddress): no memory is allocated and no allocating routine is
  * called.  Inputs whose B*H*N*(D+1) floats exceed the array return
- * SMA_ERR_ARG.  Calls sharing a device share the array: order them on one
- * stream.  No reference counterpart.
+ * SMA_ERR_ARG (dtype, head dim and sequence length are checked first, with
+ * the codes of sma_attn_bwd).  Calls sharing a device share the array: order
+ * them on one stream.  The 32 MiB are part of the library's module image, so
+ * they are reserved on every device where the module is loaded, whether or
+ * not this entry point is ever called.  No reference counterpart.
  */
 SMA_API int sma_attn_bwd_noalloc(int dtype, const void* q, const void* k, const void* v, const void* out,
                                  const void* dout, const float* lse, const void* mask_packed, void* dq, void* dk,

@@ -8,7 +8,12 @@ flags of the reference's JIT build (run.py:129-147: -O3 --use_fast_math)
 retargeted to sm_100a.  Outputs go to oracle/_ref/ only (git-ignored; the
 built .so travels with the working tree to GPU machines).
 
-    python oracle/build_ref.py [--reference /root/reference]
+    python oracle/build_ref.py --reference <reference root>
+    (or SMA_REFERENCE_ROOT=<reference root> python oracle/build_ref.py)
+
+The root the library was built from is recorded in oracle/_ref/reference_root.txt
+(tests that import the reference's Python module on the CPU machine read it
+there; GPU machines have no copy of the reference and do not need it).
 """
 
 import argparse
@@ -19,17 +24,28 @@ import subprocess
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT_DIR = os.path.join(HERE, "_ref")
 LIB = os.path.join(OUT_DIR, "libref_sma.so")
-DEFAULT_REFERENCE = "/root/reference"
+ROOT_RECORD = os.path.join(OUT_DIR, "reference_root.txt")
 
 
-def build(reference=DEFAULT_REFERENCE, force=False):
+def recorded_reference_root():
+    """The reference root of the last build, if it is still present here."""
+    if not os.path.exists(ROOT_RECORD):
+        return None
+    with open(ROOT_RECORD) as f:
+        root = f.read().strip()
+    return root if os.path.isdir(os.path.join(root, "python")) else None
+
+
+def build(reference, force=False):
     csrc = os.path.join(reference, "csrc")
     ref_cu = os.path.join(csrc, "sparse_attention.cu")
     shim = os.path.join(HERE, "ref_shim.cu")
     inputs = [ref_cu, os.path.join(csrc, "sparse_attention.h"), os.path.join(csrc, "utils.cuh"), shim]
+    os.makedirs(OUT_DIR, exist_ok=True)
+    with open(ROOT_RECORD, "w") as f:
+        f.write(os.path.abspath(reference) + "\n")
     if not force and os.path.exists(LIB) and os.path.getmtime(LIB) >= max(os.path.getmtime(p) for p in inputs):
         return LIB
-    os.makedirs(OUT_DIR, exist_ok=True)
     nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
     cmd = [
         nvcc, "-O3", "--use_fast_math", "-std=c++17",
@@ -43,17 +59,20 @@ def build(reference=DEFAULT_REFERENCE, force=False):
     return LIB
 
 
-def build_if_available(reference=DEFAULT_REFERENCE):
+def build_if_available(reference):
     """Build when the reference sources are present; otherwise keep whatever
     prebuilt library is already in oracle/_ref/ (GPU machines have no mount)."""
-    if os.path.isdir(os.path.join(reference, "csrc")):
+    if reference and os.path.isdir(os.path.join(reference, "csrc")):
         return build(reference)
     return LIB if os.path.exists(LIB) else None
 
 
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=DEFAULT_REFERENCE)
+    ap.add_argument("--reference", default=os.environ.get("SMA_REFERENCE_ROOT"),
+                    help="root of the reference checkout (default: $SMA_REFERENCE_ROOT)")
     ap.add_argument("--force", action="store_true")
     a = ap.parse_args()
+    if not a.reference:
+        ap.error("name the reference root with --reference or SMA_REFERENCE_ROOT")
     print(build(a.reference, a.force))

@@ -53,7 +53,6 @@ constexpr int kT = 128;  // query rows and keys per tile
 constexpr int kTmemCols = 512;
 constexpr uint32_t kColS = 0, kColDP = 128, kColDV = 256;
 constexpr float kLog2e = 1.44269504088896340736f;
-constexpr int kMaxDevices = 64;
 
 // Per head dim.  Tiles of K, V, Q, dO are kT rows of D/64 128-byte swizzle
 // chunks.  D = 64 double-buffers K/V (the next item's keys load while the
@@ -906,27 +905,16 @@ int launch(const BwdParams& p, const char** msg) {
     *msg = "backward: cuTensorMapEncodeTiled failed (pointer alignment or driver entry point)";
     return kErrCuda;
   }
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
-    *msg = "backward: no current CUDA device";
-    return kErrCuda;
-  }
-  static bool smem_set[kMaxDevices] = {};
-  static int sms[kMaxDevices] = {};
+  DeviceProps dp;
+  if (!device_props(&dp, msg)) return kErrCuda;
+  static std::atomic<bool> smem_set[kMaxDevices] = {};
   auto kern = attn_bwd_kernel<D, BF16>;
-  if (sms[dev] == 0 && cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
-    sms[dev] = 0;
-    *msg = "backward: cannot query the SM count";
-    return kErrCuda;
-  }
-  if (!smem_set[dev]) {
-    cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(C::kSmemBytes));
+  {
+    cudaError_t e = ensure_smem_limit(kern, C::kSmemBytes, dp.device, smem_set);
     if (e != cudaSuccess) {
       *msg = cudaGetErrorString(e);
       return kErrLaunch;
     }
-    smem_set[dev] = true;
   }
   const int64_t rows = BH * N;
   bwd_delta_kernel<D, BF16><<<static_cast<unsigned>((rows * (D / 8) + 255) / 256), 256, 0, p.stream>>>(
@@ -937,7 +925,7 @@ int launch(const BwdParams& p, const char** msg) {
     const int vec = (W % 4 == 0 && (reinterpret_cast<uintptr_t>(p.mask) & 15u) == 0) ? 1 : 0;
     // One CTA per SM (over half of its shared memory and all 512 TMEM columns each).
     const int64_t items = BH * KT;
-    const int64_t grid = items < sms[dev] ? items : sms[dev];
+    const int64_t grid = items < dp.sms ? items : dp.sms;
     kern<<<static_cast<unsigned>(grid), C::kThreads, C::kSmemBytes, p.stream>>>(
         mq, mk, mv, mdo, mdq, p.mask, p.lse, p.delta, static_cast<uint16_t*>(p.dk),
         static_cast<uint16_t*>(p.dv), static_cast<int>(N), static_cast<int>(W), static_cast<int>(KT),

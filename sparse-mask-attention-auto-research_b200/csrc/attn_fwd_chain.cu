@@ -91,7 +91,6 @@ struct ChainCfg {
 constexpr float kRescaleThreshold = 8.0f;
 constexpr float kLn2 = 0.69314718055994530942f;
 constexpr float kLog2e = 1.44269504088896340736f;
-constexpr int kMaxDevices = 64;
 
 struct ChainCtl {
   uint64_t sched_full[kSlots];
@@ -971,37 +970,22 @@ int launch(const AttnParams& p, const char** msg) {
     *msg = "attention: cuTensorMapEncodeTiled failed (pointer alignment or driver entry point)";
     return kErrCuda;
   }
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
-    *msg = "attention: no current CUDA device";
-    return kErrCuda;
-  }
-  static int sms[kMaxDevices] = {};
-  static bool smem_set[kMaxDevices] = {};
-  if (sms[dev] == 0 && cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
-    *msg = "attention: cannot query the SM count";
-    return kErrCuda;
-  }
+  DeviceProps dp;
+  if (!device_props(&dp, msg)) return kErrCuda;
+  static std::atomic<bool> smem_set[kMaxDevices] = {};
   auto kern = attn_fwd_chain_kernel<D, BF16>;
-  if (!smem_set[dev]) {
-    cudaError_t e =
-        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(kSmemBytes));
+  {
+    cudaError_t e = ensure_smem_limit(kern, kSmemBytes, dp.device, smem_set);
     if (e != cudaSuccess) {
       *msg = cudaGetErrorString(e);
       return kErrLaunch;
     }
-    smem_set[dev] = true;
   }
   const int vec = (W % 4 == 0 && (reinterpret_cast<uintptr_t>(p.mask) & 15u) == 0) ? 1 : 0;
   const int o_wide = (reinterpret_cast<uintptr_t>(p.out) & 31u) == 0 ? 1 : 0;  // 32-byte O stores (D = 128)
   // Head-major item order once K and V of all heads exceed half of L2.
-  static int l2_bytes[kMaxDevices] = {};
-  if (l2_bytes[dev] == 0 && cudaDeviceGetAttribute(&l2_bytes[dev], cudaDevAttrL2CacheSize, dev) != cudaSuccess) {
-    *msg = "attention: cannot query the L2 size";
-    return kErrCuda;
-  }
-  const int head_major = 2 * BH * N * D * 2 > l2_bytes[dev] / 2 ? 1 : 0;
-  const int grid = static_cast<int>(total < sms[dev] ? total : sms[dev]);
+  const int head_major = 2 * BH * N * D * 2 > dp.l2_bytes / 2 ? 1 : 0;
+  const int grid = static_cast<int>(total < dp.sms ? total : dp.sms);
   // The occupancy map describes 128-key tiles: only the D = 64 kernel uses it.
   const uint32_t* occ = D == 64 ? p.occ : nullptr;
   cudaError_t e = launch_pdl(kern, static_cast<unsigned>(grid), kThreads, kSmemBytes, p.stream, mq, mk, mv, mo,

@@ -5,8 +5,11 @@
 // Mirrors the reference pybind layer (csrc/binding.cpp:9-71), whose checks
 // (CUDA tensors, 4-D shapes, fp16/bf16 dtype) become SMA_* status codes here;
 // the Python shim turns them into RuntimeError like TORCH_CHECK does.
+#include <atomic>
 #include <cstdio>
 #include <string>
+
+#include <nvtx3/nvToolsExt.h>
 
 #include "sma_capi.h"
 #include "sma_internal.h"
@@ -14,13 +17,25 @@
 namespace {
 
 thread_local std::string g_last_error;
-uint64_t g_timeout_ns = 2000000000ull;
+std::atomic<uint64_t> g_timeout_ns{2000000000ull};
+
+// NVTX range over one entry point (host side: argument checks and launches).
+// nvtx3 is header-only and costs a branch when no profiler is attached.
+struct NvtxRange {
+  explicit NvtxRange(const char* name) { nvtxRangePushA(name); }
+  ~NvtxRange() { nvtxRangePop(); }
+  NvtxRange(const NvtxRange&) = delete;
+  NvtxRange& operator=(const NvtxRange&) = delete;
+};
 
 // Device word the kernels OR error bits into (one instance per device).
 __device__ uint32_t g_device_error_word;
 
-constexpr int kMaxDevices = 64;
-uint32_t* g_err_ptr[kMaxDevices] = {};
+using sma::kMaxDevices;
+// Per-device address caches.  Several host threads may fill an entry on their
+// first call; they all store the same value, and the atomics make that
+// well-defined.
+std::atomic<uint32_t*> g_err_ptr[kMaxDevices] = {};
 
 int fail(int code, const char* msg) {
   g_last_error = msg ? msg : "unknown error";
@@ -38,13 +53,15 @@ int error_word(uint32_t** out) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices) return fail(sma::kErrCuda, "device index out of range");
-  if (g_err_ptr[dev] == nullptr) {
+  uint32_t* ptr = g_err_ptr[dev].load(std::memory_order_relaxed);
+  if (ptr == nullptr) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_device_error_word);
     if (e != cudaSuccess) return fail_cuda(e, "cudaGetSymbolAddress");
-    g_err_ptr[dev] = static_cast<uint32_t*>(p);
+    ptr = static_cast<uint32_t*>(p);
+    g_err_ptr[dev].store(ptr, std::memory_order_relaxed);
   }
-  *out = g_err_ptr[dev];
+  *out = ptr;
   return sma::kOk;
 }
 
@@ -52,10 +69,12 @@ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) ==
 
 // Fixed device scratch of sma_attn_bwd_noalloc: the FP32 dQ accumulator
 // (B*H*N*D floats) followed by Delta (B*H*N floats).  One copy per device,
-// part of the module image, so that entry point allocates nothing.
+// part of the module image (so it is reserved on every device where the
+// library's module is loaded, whether or not the entry point is called),
+// so that entry point allocates nothing.
 constexpr int64_t kNoAllocScratchFloats = int64_t{8} << 20;  // 32 MiB
 static __device__ __align__(256) float g_bwd_noalloc_scratch[kNoAllocScratchFloats];
-float* g_noalloc_ptr[kMaxDevices] = {};
+std::atomic<float*> g_noalloc_ptr[kMaxDevices] = {};
 
 // Device address of the fixed scratch on the current device (looked up once per device).
 int noalloc_scratch(float** out) {
@@ -63,13 +82,15 @@ int noalloc_scratch(float** out) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices) return fail(sma::kErrCuda, "device index out of range");
-  if (g_noalloc_ptr[dev] == nullptr) {
+  float* ptr = g_noalloc_ptr[dev].load(std::memory_order_relaxed);
+  if (ptr == nullptr) {
     void* p = nullptr;
     e = cudaGetSymbolAddress(&p, g_bwd_noalloc_scratch);
     if (e != cudaSuccess) return fail_cuda(e, "cudaGetSymbolAddress");
-    g_noalloc_ptr[dev] = static_cast<float*>(p);
+    ptr = static_cast<float*>(p);
+    g_noalloc_ptr[dev].store(ptr, std::memory_order_relaxed);
   }
-  *out = g_noalloc_ptr[dev];
+  *out = ptr;
   return sma::kOk;
 }
 
@@ -78,6 +99,7 @@ int noalloc_scratch(float** out) {
 extern "C" {
 
 int sma_pack_mask(const void* mask, void* packed, int64_t B, int64_t H, int64_t N, void* stream) {
+  NvtxRange range("sma_pack_mask");
   if (B < 0 || H < 0 || N < 0) return fail(sma::kErrArg, "pack_mask: negative dimension");
   if (B == 0 || H == 0 || N == 0) return sma::kOk;
   if (mask == nullptr || packed == nullptr) return fail(sma::kErrArg, "pack_mask: null pointer");
@@ -94,6 +116,7 @@ namespace {
 int attn_fwd_impl(int dtype, const void* q, const void* k, const void* v, const void* mask_packed,
                   const uint32_t* occupancy, void* out, float* lse, int64_t B, int64_t H, int64_t N, int64_t D,
                   float scale, void* stream) {
+  NvtxRange range("sma_attn_fwd");
   if (dtype != SMA_DTYPE_FP16 && dtype != SMA_DTYPE_BF16)
     return fail(sma::kErrDtype, "attention: unsupported dtype, need fp16 or bf16");
   if (B < 0 || H < 0 || N < 0 || D <= 0) return fail(sma::kErrArg, "attention: bad dimension");
@@ -127,7 +150,7 @@ int attn_fwd_impl(int dtype, const void* q, const void* k, const void* v, const 
   p.D = D;
   p.scale = scale;
   p.err_word = err;
-  p.timeout_ns = g_timeout_ns;
+  p.timeout_ns = g_timeout_ns.load(std::memory_order_relaxed);
   p.stream = static_cast<cudaStream_t>(stream);
   const char* msg = nullptr;
   rc = sma::launch_attn_fwd(p, &msg);
@@ -145,6 +168,7 @@ int sma_attn_fwd(int dtype, const void* q, const void* k, const void* v, const v
 
 int sma_pack_mask_occupancy(const void* mask, void* packed, void* occupancy, int64_t B, int64_t H, int64_t N,
                             void* stream) {
+  NvtxRange range("sma_pack_mask_occupancy");
   if (B < 0 || H < 0 || N < 0) return fail(sma::kErrArg, "pack_mask_occupancy: negative dimension");
   if (N > SMA_MAX_SEQ_LEN_OCCUPANCY)
     return fail(sma::kErrUnsupportedN, "pack_mask_occupancy: sequence length above the occupancy map's maximum (8192)");
@@ -169,6 +193,7 @@ int sma_attn_fwd_occupancy(int dtype, const void* q, const void* k, const void* 
 int sma_attn_bwd(int dtype, const void* q, const void* k, const void* v, const void* out, const void* dout,
                  const float* lse, const void* mask_packed, void* dq, void* dk, void* dv, float* dq_accum, float* delta,
                  int64_t B, int64_t H, int64_t N, int64_t D, float scale, void* stream) {
+  NvtxRange range("sma_attn_bwd");
   if (dtype != SMA_DTYPE_FP16 && dtype != SMA_DTYPE_BF16)
     return fail(sma::kErrDtype, "backward: unsupported dtype, need fp16 or bf16");
   if (B < 0 || H < 0 || N < 0 || D <= 0) return fail(sma::kErrArg, "backward: bad dimension");
@@ -207,7 +232,7 @@ int sma_attn_bwd(int dtype, const void* q, const void* k, const void* v, const v
   p.D = D;
   p.scale = scale;
   p.err_word = err;
-  p.timeout_ns = g_timeout_ns;
+  p.timeout_ns = g_timeout_ns.load(std::memory_order_relaxed);
   p.stream = static_cast<cudaStream_t>(stream);
   const char* msg = nullptr;
   rc = sma::launch_attn_bwd(p, &msg);
@@ -217,12 +242,17 @@ int sma_attn_bwd(int dtype, const void* q, const void* k, const void* v, const v
 int sma_attn_bwd_noalloc(int dtype, const void* q, const void* k, const void* v, const void* out, const void* dout,
                          const float* lse, const void* mask_packed, void* dq, void* dk, void* dv, int64_t B,
                          int64_t H, int64_t N, int64_t D, float scale, void* stream) {
+  // The checks of sma_attn_bwd, with its codes, come first; then the size
+  // of the fixed scratch.
+  if (dtype != SMA_DTYPE_FP16 && dtype != SMA_DTYPE_BF16)
+    return fail(sma::kErrDtype, "backward: unsupported dtype, need fp16 or bf16");
   if (B < 0 || H < 0 || N < 0 || D <= 0) return fail(sma::kErrArg, "backward: bad dimension");
+  if (D != 64 && D != 128) return fail(sma::kErrUnsupportedD, "backward: head dim must be 64 or 128");
+  if (N > SMA_MAX_SEQ_LEN) return fail(sma::kErrUnsupportedN, "backward: sequence length above the supported maximum (65536)");
   if (B == 0 || H == 0 || N == 0) return sma::kOk;
   // dQ accumulator + Delta must fit the fixed scratch (checked without overflow).
   const int64_t per_bh = N * (D + 1);
-  if (D > 4096 || N > SMA_MAX_SEQ_LEN || B > kNoAllocScratchFloats || H > kNoAllocScratchFloats ||
-      B * H > kNoAllocScratchFloats / per_bh)
+  if (B > kNoAllocScratchFloats || H > kNoAllocScratchFloats || B * H > kNoAllocScratchFloats / per_bh)
     return fail(sma::kErrArg, "backward (no-alloc): B*H*N*(D+1) floats exceed the fixed 32 MiB scratch");
   float* scratch = nullptr;
   int rc = noalloc_scratch(&scratch);
@@ -238,12 +268,13 @@ int sma_device_status(void* stream, int clear) {
   cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail_cuda(e, "cudaStreamSynchronize");
   uint32_t v = 0;
-  e = cudaMemcpy(&v, err, sizeof(v), cudaMemcpyDeviceToHost);
+  e = cudaMemcpyAsync(&v, err, sizeof(v), cudaMemcpyDeviceToHost, static_cast<cudaStream_t>(stream));
+  if (e == cudaSuccess) e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail_cuda(e, "read device error word");
   if (clear) {
-    e = cudaMemset(err, 0, sizeof(uint32_t));
-    if (e != cudaSuccess) return fail_cuda(e, "clear device error word");
-    e = cudaDeviceSynchronize();
+    // Ordered on the caller's stream, so other streams of the device keep running.
+    e = cudaMemsetAsync(err, 0, sizeof(uint32_t), static_cast<cudaStream_t>(stream));
+    if (e == cudaSuccess) e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
     if (e != cudaSuccess) return fail_cuda(e, "clear device error word");
   }
   if (v & sma::kDevErrTimeout) return fail(sma::kErrTimeout, "a device-side wait timed out");
@@ -253,7 +284,7 @@ int sma_device_status(void* stream, int clear) {
 
 int sma_set_wait_timeout_ns(uint64_t ns) {
   if (ns == 0) return fail(sma::kErrArg, "timeout must be positive");
-  g_timeout_ns = ns;
+  g_timeout_ns.store(ns, std::memory_order_relaxed);
   return sma::kOk;
 }
 

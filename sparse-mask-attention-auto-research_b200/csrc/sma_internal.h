@@ -2,6 +2,7 @@
 // C-ABI layer (sma_capi.cu).  Nothing here is exported from the library.
 #pragma once
 
+#include <atomic>
 #include <cstdint>
 #include <cuda.h>
 #include <cuda_runtime.h>
@@ -74,7 +75,7 @@ struct BwdParams {
   cudaStream_t stream;
 };
 
-// Backward (attn_bwd.cu): head dim 64.
+// Backward (attn_bwd.cu): head dims 64 and 128.
 int launch_attn_bwd(const BwdParams& p, const char** msg);
 
 // TMA map of the [BH, N, D] view of a contiguous [B, H, N, D] fp16/bf16
@@ -84,6 +85,28 @@ bool make_tensor_map_3d(CUtensorMap* m, const void* ptr, int dtype, int64_t D, i
 // The same view of a contiguous FP32 [BH, N, D] tensor: boxes of 32 elements
 // (128 bytes) by `rows` rows, 128-byte swizzle (tma_map.cu).
 bool make_tensor_map_3d_f32(CUtensorMap* m, const void* ptr, int64_t D, int64_t BH, int64_t N, int rows);
+
+// Devices the per-device caches of the launchers cover.
+constexpr int kMaxDevices = 64;
+
+// Properties of the current device, queried once per device (thread-safe).
+struct DeviceProps {
+  int device = -1;
+  int sms = 0;
+  int l2_bytes = 0;
+};
+bool device_props(DeviceProps* out, const char** msg);
+
+// Raises `kern`'s dynamic shared-memory limit to `bytes` on the current
+// device the first time it is launched there.  `done` is the kernel's own
+// per-device flag array; concurrent first calls both set the same attribute.
+template <typename Kern>
+cudaError_t ensure_smem_limit(Kern kern, size_t bytes, int dev, std::atomic<bool> (&done)[kMaxDevices]) {
+  if (done[dev].load(std::memory_order_relaxed)) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes));
+  if (e == cudaSuccess) done[dev].store(true, std::memory_order_relaxed);
+  return e;
+}
 
 // Launches `kern` with programmatic stream serialisation: its CTAs may start
 // (and run their set-up) while the previous kernel in the stream finishes;

@@ -1,26 +1,59 @@
-// TMA tensor maps for the attention kernels.  The driver entry point is
-// reached through the runtime (cudaGetDriverEntryPoint), so the library does
-// not link libcuda.
+// Host-side helpers of the kernel launchers: TMA tensor maps and per-device
+// properties.  The driver entry point is reached through the runtime
+// (cudaGetDriverEntryPoint), so the library does not link libcuda.
 #include <cudaTypedefs.h>
+
+#include <mutex>
 
 #include "sma_internal.h"
 
 namespace sma {
 namespace {
 
+PFN_cuTensorMapEncodeTiled_v12000 lookup_encode_fn() {
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+      q == cudaDriverEntryPointSuccess)
+    return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  return nullptr;
+}
+
+// Looked up once per process (a function-local static is initialised once,
+// even with several host threads).
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (fn == nullptr) {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
+  static const PFN_cuTensorMapEncodeTiled_v12000 fn = lookup_encode_fn();
   return fn;
 }
 
+struct DeviceSlot {
+  std::once_flag once;
+  DeviceProps props;
+  bool ok = false;
+};
+DeviceSlot g_devices[kMaxDevices];
+
 }  // namespace
+
+bool device_props(DeviceProps* out, const char** msg) {
+  int dev = -1;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+    *msg = "no current CUDA device (or device index out of range)";
+    return false;
+  }
+  DeviceSlot& s = g_devices[dev];
+  std::call_once(s.once, [&]() {
+    s.props.device = dev;
+    s.ok = cudaDeviceGetAttribute(&s.props.sms, cudaDevAttrMultiProcessorCount, dev) == cudaSuccess &&
+           cudaDeviceGetAttribute(&s.props.l2_bytes, cudaDevAttrL2CacheSize, dev) == cudaSuccess && s.props.sms > 0;
+  });
+  if (!s.ok) {
+    *msg = "cannot query the SM count / L2 size of the current device";
+    return false;
+  }
+  *out = s.props;
+  return true;
+}
 
 bool make_tensor_map_3d(CUtensorMap* m, const void* ptr, int dtype, int64_t D, int64_t BH, int64_t N, int rows) {
   auto fn = encode_fn();

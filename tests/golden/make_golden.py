@@ -1,9 +1,10 @@
 """Generate the golden fixtures in tests/golden/ by running the reference's
 own CPU code (yulangz/sparse-mask-attention-auto-research, python/sparse_attention.py).
 
-Run in a container where the reference is mounted (default /root/reference):
+Run in a container where the reference is mounted, naming its root:
 
-    python tests/golden/make_golden.py [--reference /root/reference]
+    python tests/golden/make_golden.py --reference <reference root>
+    (or SMA_REFERENCE_ROOT=<reference root> python tests/golden/make_golden.py)
 
 The reference module is imported read-only; with no compiled extension it
 takes its CPU paths:
@@ -107,8 +108,11 @@ def qkv(gen, B, H, N, D, dtype, mult=1.0):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", default=os.environ.get("SMA_REFERENCE_ROOT"),
+                    help="root of the reference checkout (default: $SMA_REFERENCE_ROOT)")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("name the reference root with --reference or SMA_REFERENCE_ROOT")
     sys.path.insert(0, args.reference)
     import importlib
 

@@ -153,6 +153,13 @@ def test_bwd_noalloc_rejects_problems_beyond_its_scratch(lib):
 
     assert call(1, 256, 512, 64) == L.SMA_ERR_ARG  # 256*512*65 floats > 8 Mi
     assert b"scratch" in lib.sma_last_error()
-    assert call(1, 1, L.SMA_MAX_SEQ_LEN + 1, 64) == L.SMA_ERR_ARG
+    # The argument checks of sma_attn_bwd come first, with its codes.
+    assert call(1, 1, L.SMA_MAX_SEQ_LEN + 1, 64) == L.SMA_ERR_UNSUPPORTED_N
+    assert call(1, 1, 64, 96) == L.SMA_ERR_UNSUPPORTED_D
+    assert lib.sma_attn_bwd_noalloc(7, 16, 16, 16, 16, 16, 16, 16, 16, 16, 16, 64, 64, 1024, 64, 0.125,
+                                    None) == L.SMA_ERR_DTYPE
     assert call(-1, 1, 64, 64) == L.SMA_ERR_ARG
     assert call(0, 1, 64, 64) == L.SMA_OK
+    # Largest accepted size: B*H*N*(D+1) just under 8 Mi floats; one more head is rejected.
+    heads = (8 << 20) // (512 * 65)
+    assert call(1, heads + 1, 512, 64) == L.SMA_ERR_ARG

@@ -11,7 +11,7 @@ import os
 import pytest
 import torch
 
-from conftest import FLT_MAX, LSE_TOL, OUT_TOL, REPO, ulp
+from conftest import FLT_MAX, LSE_TOL, OUT_TOL, REPO, record_parity, ulp
 from python import pack_mask, sparse_attn_cuda, workloads
 
 pytestmark = pytest.mark.gpu
@@ -56,6 +56,7 @@ def test_matches_reference_kernel(ref, name):
     diff = (out.float() - out_ref.float()).abs()
     bound = OUT_TOL[q.dtype] + ulp(out_ref.float(), q.dtype)
     err = diff.max().item()
+    record_parity(f"{name} vs reference CUDA kernel", max_abs_out=err)
     assert (diff <= bound).all(), f"{name}: max |ours - reference kernel| = {err}"
     empty = lse_ref == -FLT_MAX
     assert torch.equal(empty, lse == -FLT_MAX)
