@@ -55,6 +55,13 @@ namespace {
 
 constexpr int kBM = 128;
 constexpr int kThreads = 384;
+// Register split after start-up: the launch gives every thread 168 (384 x
+// 168 = 64512); the loader and MMA warps (one warpgroup) drop to 64 and the
+// two softmax warpgroups rise to 216: 128 x 64 + 256 x 216 = 63488 <= 64512.
+constexpr int kRegsLaunch = 168;
+constexpr int kRegsOther = 64;
+constexpr int kRegsSoftmax = 216;
+static_assert(128 * kRegsOther + 256 * kRegsSoftmax <= kThreads * kRegsLaunch, "register split");
 constexpr int kSlots = 4;          // live-list slots per chain
 constexpr int kMaxSeq = 65536;     // longest sequence the live-tile bitsets cover
 constexpr int kLiveWords = kMaxSeq / 64 / 32;  // bit words per item: one bit per key tile (64 keys or more)
@@ -396,6 +403,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 8 || warp == 9) {
     // ================================================================ loader
+    regs_dec<kRegsOther>();
     const int c = warp - 8;
     ChainCtl& cc = ctl.ch[c];
     if (lane == 0) {
@@ -488,6 +496,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else if (warp == 10 || warp == 11) {
     // ================================================================ MMA issuer
+    regs_dec<kRegsOther>();
     const int c = warp - 10;
     ChainCtl& cc = ctl.ch[c];
     if (lane == 0) {
@@ -577,6 +586,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     // ================================================================ softmax
+    regs_inc<kRegsSoftmax>();
     const int c = warp >> 2;
     const int wq = warp & 3;
     ChainCtl& cc = ctl.ch[c];
