@@ -401,6 +401,44 @@ __global__ void __launch_bounds__(kThreads, 1)
     return 0;
   };
 
+  // The loader and the MMA warp look one live tile ahead: the next K copy
+  // and QK^T go before this tile's V copy and PV.  Past an item with no live
+  // tile, though, the next live tile lies in an item whose list the softmax
+  // publishes only after this tile's PV, so waiting for it first would
+  // deadlock.  look_ahead() decides, without changing the cursor: 1 = the
+  // next live tile needs no list that is not out (same item, or the next
+  // item's list is published with a live tile, or no items left); -1 = the
+  // next item's list is out and has no live tile (finish this tile first);
+  // 0 = not known yet.  Callers poll it together with the readiness of
+  // their own next step and take whichever comes first.
+  auto look_ahead = [&](ChainCtl& cc, const Cursor& cu, int n_items) -> int {
+    if (cu.i >= 0 && cu.i < n_items && cu.t + 1 < cu.n) return 1;
+    const int j = cu.i + 1;
+    if (j >= n_items) return 1;
+    const int slot = j % kSlots;
+    if (!mbar_test_wait(smem_u32(&cc.sched_full[slot]), (j / kSlots) & 1)) return 0;
+    return cc.n_live[slot] != 0u ? 1 : -1;
+  };
+  // Polls look_ahead() and `own_ready` (the caller's own next step can go
+  // without waiting) until one decides: true = look ahead first, false =
+  // finish this tile first.  Bounded like every wait; `ok` turns false when
+  // it gives up.
+  auto decide_ahead = [&](ChainCtl& cc, const Cursor& cu, int n_items, auto own_ready, bool& ok) -> bool {
+    const int a0 = look_ahead(cc, cu, n_items);  // the common case decides at once
+    if (a0 != 0) return a0 > 0;
+    const uint64_t t0 = global_timer_ns();
+    for (;;) {
+      const int a = look_ahead(cc, cu, n_items);
+      if (a != 0) return a > 0;
+      if (own_ready()) return false;
+      if (*abort_flag != 0u || global_timer_ns() - t0 > timeout_ns) {
+        ok = false;
+        return false;
+      }
+      __nanosleep(32);
+    }
+  };
+
   if (warp == 8 || warp == 9) {
     // ================================================================ loader
     regs_dec<kRegsOther>();
@@ -462,16 +500,21 @@ __global__ void __launch_bounds__(kThreads, 1)
         ++gv;
         return true;
       };
-      int rk = advance(cc, kc, n_items, false);
+      // The K cursor walks the live tiles and releases every item it leaves
+      // (so no list slot is reused before it has passed); the V copy of a
+      // tile uses the K cursor's position saved when that tile's K was issued.
+      int rk = advance(cc, kc, n_items, true);
       if (rk < 0 || (rk == 1 && !issue_k())) ok = false;
-      while (ok) {
-        const int rv = advance(cc, vc, n_items, true);
-        if (rv <= 0) {
-          ok = rv == 0;
-          break;
-        }
-        if (rk == 1) {
-          rk = advance(cc, kc, n_items, false);
+      while (ok && rk == 1) {
+        vc = kc;  // tile g: its K is out, its V is next
+        // K of the next live tile before this V, unless that waits on the softmax.
+        const bool k_first = decide_ahead(cc, kc, n_items, [&]() {
+          return gv < static_cast<uint32_t>(kStages) ||
+                 mbar_test_wait(smem_u32(&cc.v_empty[gv % kStages]), ((gv / kStages) - 1) & 1);
+        }, ok);
+        if (!ok) break;
+        if (k_first) {
+          rk = advance(cc, kc, n_items, true);
           if (rk < 0 || (rk == 1 && !issue_k())) {
             ok = false;
             break;
@@ -481,7 +524,15 @@ __global__ void __launch_bounds__(kThreads, 1)
           ok = false;
           break;
         }
+        if (!k_first) {
+          rk = advance(cc, kc, n_items, true);
+          if (rk < 0 || (rk == 1 && !issue_k())) {
+            ok = false;
+            break;
+          }
+        }
       }
+      if (rk < 0) ok = false;
       if (!ok) {
         fail();
         // Let the copies this thread started land before the CTA exits.
@@ -553,13 +604,23 @@ __global__ void __launch_bounds__(kThreads, 1)
       int res = advance_qk();
       if (res < 0 || (res == 1 && !issue_qk(0))) ok = false;
       if (ok && res == 1) n_qk = 1;
-      for (uint32_t g = 0; ok && g < n_qk; ++g) {
+      // QK^T of the next live tile; returns false if a wait gave up.
+      auto qk_ahead = [&](uint32_t g) -> bool {
         res = advance_qk();
-        if (res < 0 || (res == 1 && !issue_qk(g + 1))) {
+        if (res < 0 || (res == 1 && !issue_qk(g + 1))) return false;
+        if (res == 1) ++n_qk;
+        return true;
+      };
+      for (uint32_t g = 0; ok && g < n_qk; ++g) {
+        // The next QK^T before this PV, unless that waits on the softmax.
+        const bool qk_first = decide_ahead(cc, qc, n_items, [&]() {
+          return mbar_test_wait(smem_u32(&cc.p_full), g & 1);
+        }, ok);
+        if (!ok) break;
+        if (qk_first && !qk_ahead(g)) {
           ok = false;
           break;
         }
-        if (res == 1) ++n_qk;
         const int stage = g % kStages;
         if (!mbar_wait_bounded(smem_u32(&cc.p_full), g & 1, abort_flag, timeout_ns) ||
             !mbar_wait_bounded(smem_u32(&cc.v_full[stage]), (g / kStages) & 1, abort_flag, timeout_ns)) {
@@ -577,6 +638,10 @@ __global__ void __launch_bounds__(kThreads, 1)
                  (fresh && kk == 0) ? 0u : 1u);
         mma_commit(smem_u32(&cc.pv_done));
         mma_commit(smem_u32(&cc.v_empty[stage]));
+        if (!qk_first && !qk_ahead(g)) {
+          ok = false;
+          break;
+        }
       }
       if (!ok) fail();
       // Every MMA this thread issued must complete before TMEM is released.

@@ -206,3 +206,39 @@ def test_unsupported_head_dim_raises():
     m = torch.ones(1, 1, 64, 64, dtype=torch.bool, device=DEV)
     with pytest.raises(RuntimeError, match="head dim"):
         sparse_attention(q, q, q, m)
+
+
+@pytest.mark.parametrize("name,empty_rounds", [("c1", (1,)), ("c5", (1, 2)), ("c5", (1, 2, 3, 4, 5))])
+def test_items_without_live_tiles_between_live_items(name, empty_rounds):
+    """Work items with no set mask bit between live ones.  The kernel runs
+    items round by round over two chains per SM (chain k of G CTAs takes
+    item k, then 4G-1-k, then 4G+k, ...), so emptying whole rounds gives
+    every chain one, two or five empty items in a row.  Its loader and MMA
+    warps look one live tile ahead, past the empty items, into a list the
+    softmax publishes only after the current item's last product; they must
+    finish the current tile first instead of waiting for it, and the lists
+    of the items between must not wait for list slots held by the current
+    item."""
+    q, k, v, m = workloads.make_inputs(name, seed=12, device=DEV)
+    B, H, N, D = q.shape
+    BH, QT = B * H, N // 128
+    props = torch.cuda.get_device_properties(0)
+    G = min(BH * QT, props.multi_processor_count)
+    # The kernel's item order: batch*head fastest while K and V of all heads
+    # fit in half of L2, query tiles of a head consecutive otherwise.
+    head_major = 2 * BH * N * D * 2 > props.L2_cache_size // 2
+    m = m.reshape(BH, N, N)
+    for rnd in empty_rounds:
+        for w in range(2 * G * rnd, min(2 * G * (rnd + 1), BH * QT)):
+            if head_major:
+                bh, qt = w // QT, QT - 1 - w % QT
+            else:
+                bh, qt = w % BH, QT - 1 - w // BH
+            m[bh, qt * 128:(qt + 1) * 128, :] = False
+    m = m.reshape(B, H, N, N)
+    out, lse = run_fwd(q, k, v, m)
+    heads = torch.arange(0, BH, 5 if BH <= 768 else 61, device=DEV)
+    qf, kf, vf, mf = (x.reshape(BH, N, -1)[heads].float().cpu().numpy() for x in (q, k, v, m))
+    ref_out, ref_lse = oracle.attention_parallel(qf, kf, vf, mf.astype(bool), 1 / math.sqrt(D), with_lse=True)
+    check_against(out.reshape(BH, N, D)[heads], lse.reshape(BH, N)[heads], torch.from_numpy(ref_out),
+                  torch.from_numpy(ref_lse), torch.from_numpy(mf.astype(bool)), q.dtype)
