@@ -180,3 +180,31 @@ def test_backward_skipped_tiles_do_not_touch_garbage(D, dtype):
     assert torch.equal(dirty[2][..., live_k, :], clean[2][..., live_k, :])
     for x in dirty:
         assert not torch.isnan(x).any()
+
+
+@pytest.mark.parametrize("empty_rounds", [(1,), (1, 2, 3)])
+def test_items_without_live_tiles_between_live_items(empty_rounds):
+    """Backward work items (batch*head, 128-key tile) that no query row
+    attends, between live ones.  CTA c of G takes items c, c + G, c + 2G, ...,
+    so emptying whole rounds of items gives every CTA one or three empty
+    items in a row; their lists are published by the scanner warp while the
+    other warps are still on the live item before them."""
+    q, k, v, m = workloads.make_inputs("c1", seed=21, device=DEV)
+    B, H, N, D = q.shape
+    BH, KT = B * H, N // 128
+    G = min(BH * KT, torch.cuda.get_device_properties(0).multi_processor_count)
+    m = m.reshape(BH, N, N)
+    for rnd in empty_rounds:
+        for j in range(G * rnd, min(G * (rnd + 1), BH * KT)):
+            bh, kt = j // KT, j % KT
+            m[bh, :, kt * 128:(kt + 1) * 128] = False
+    m = m.reshape(B, H, N, N)
+    g = torch.Generator(device=DEV).manual_seed(22)
+    dout = torch.randn(q.shape, generator=g, device=DEV).to(q.dtype)
+    got = fwd_bwd(q, k, v, m, dout)
+    heads = torch.arange(0, BH, 7, device=DEV)
+    sub = [x.reshape(BH, N, D)[heads].unsqueeze(0) for x in got]
+    qf, kf, vf, df = (x.reshape(BH, N, D)[heads].unsqueeze(0).float().cpu().numpy() for x in (q, k, v, dout))
+    mf = m.reshape(BH, N, N)[heads].unsqueeze(0).cpu()
+    want = oracle.attention_backward(qf, kf, vf, mf.numpy(), 1 / math.sqrt(D), df)
+    check_grads(sub, want, q.dtype, mf)
