@@ -82,6 +82,29 @@ SMA_API int sma_attn_fwd(int dtype, const void* q, const void* k, const void* v,
                  void* stream);
 
 /*
+ * The pack + forward pair in one launch: the attention kernel reads the bool
+ * mask [B, H, N, N] (one byte per element, non-zero = attend) itself, packs
+ * each query tile's rows as it scans them for live key tiles, and writes the
+ * packed words to mask_packed ([B, H, N, N/32], bit for bit what
+ * sma_pack_mask writes, kept for the backward).  out and lse are those of
+ * sma_attn_fwd on the packed mask, bit for bit.
+ * Needs N % 32 == 0 and 16-byte aligned mask and mask_packed (SMA_ERR_ARG
+ * otherwise: callers then use sma_pack_mask + sma_attn_fwd); the rest as for
+ * sma_attn_fwd.  On B200 the pair of launches is faster (the packer streams
+ * the mask at HBM speed, while here each query tile's rows are read and
+ * packed by the softmax warps between tiles, on the kernel's critical path),
+ * so sparse_attention() uses the pair; this entry saves a launch only.
+ *
+ * Replaces: the pack_mask() + SparseAttentionFunction forward pair that
+ *           sparse_attention() runs   python/sparse_attention.py:122-156
+ *           (pack_mask_bits()         csrc/sparse_attention.cu:44-54,
+ *            forward()                csrc/binding.cpp:9-47)
+ */
+SMA_API int sma_attn_fwd_mask(int dtype, const void* q, const void* k, const void* v, const void* mask,
+                              void* mask_packed, void* out, float* lse, int64_t B, int64_t H, int64_t N, int64_t D,
+                              float scale, void* stream);
+
+/*
  * Fused bool -> bit packing plus occupancy map.  Writes `packed` exactly as
  * sma_pack_mask does and `occupancy`: uint32 [B*H, ceil(N/128), 2], where bit t
  * of the pair for (batch*head, query tile qt) is set iff key tile t (keys

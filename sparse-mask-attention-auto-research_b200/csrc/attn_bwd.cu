@@ -899,10 +899,13 @@ int launch(const BwdParams& p, const char** msg) {
     return kErrArg;
   }
   CUtensorMap mq, mk, mv, mdo, mdq;
-  if (!make_tensor_map_3d(&mq, p.q, p.dtype, D, BH, N, kT) || !make_tensor_map_3d(&mk, p.k, p.dtype, D, BH, N, kT) ||
-      !make_tensor_map_3d(&mv, p.v, p.dtype, D, BH, N, kT) || !make_tensor_map_3d(&mdo, p.dout, p.dtype, D, BH, N, kT) ||
-      !make_tensor_map_3d_f32(&mdq, p.dq_accum, D, BH, N, 32)) {
-    *msg = "backward: cuTensorMapEncodeTiled failed (pointer alignment or driver entry point)";
+  CUresult rc = make_tensor_map_3d(&mq, p.q, p.dtype, D, BH, N, kT);
+  if (rc == CUDA_SUCCESS) rc = make_tensor_map_3d(&mk, p.k, p.dtype, D, BH, N, kT);
+  if (rc == CUDA_SUCCESS) rc = make_tensor_map_3d(&mv, p.v, p.dtype, D, BH, N, kT);
+  if (rc == CUDA_SUCCESS) rc = make_tensor_map_3d(&mdo, p.dout, p.dtype, D, BH, N, kT);
+  if (rc == CUDA_SUCCESS) rc = make_tensor_map_3d_f32(&mdq, p.dq_accum, D, BH, N, 32);
+  if (rc != CUDA_SUCCESS) {
+    *msg = tensor_map_error("backward", rc);
     return kErrCuda;
   }
   DeviceProps dp;

@@ -46,6 +46,12 @@ int launch_attn_fwd(const AttnParams& p, const char** msg) {
     *msg = "attention: occupancy map given for a sequence length above 8192";
     return kErrUnsupportedN;
   }
+  if (p.bmask != nullptr && (p.N % 32 != 0 || p.packed_out == nullptr ||
+                            (reinterpret_cast<uintptr_t>(p.bmask) & 15u) != 0 ||
+                            (reinterpret_cast<uintptr_t>(p.packed_out) & 15u) != 0)) {
+    *msg = "attention: the bool-mask forward needs N % 32 == 0 and 16-byte aligned mask / packed output";
+    return kErrArg;
+  }
   if (!chain_supported(p)) {
     *msg = "attention: shape not supported by the attention kernel";
     return kErrUnsupportedN;

@@ -47,6 +47,7 @@
 #include <cuda_fp16.h>
 #include <cudaTypedefs.h>
 
+#include "mask_bits.cuh"
 #include "sma_internal.h"
 #include "sma_ptx.cuh"
 
@@ -69,6 +70,7 @@ constexpr int kStages = 2;         // K ring and V ring depth per chain
 constexpr int kTmemCols = 512;
 constexpr int kChainCols = 256;
 constexpr int kScanBatch = 4;      // 16-byte mask loads in flight per thread while scanning
+constexpr int kPackBatch = 8;      // bool input: packed words (32 mask bytes each) per batch of loads in flight
 constexpr int kEpiGroups = 8;      // D = 128: mask rows of up to 8 16-byte groups (N <= 1024) scanned from registers
 
 // Per head dim: D = 64 takes 128-key tiles, D = 128 takes 64-key tiles, so a
@@ -212,26 +214,29 @@ __device__ __forceinline__ uint32_t valid_bits(int cw, int N) {
 
 // The mask words of key tile kt (kWords of them) for one query row, columns
 // >= N cleared.
-template <int D>
+// kOwn: the words were written earlier in this kernel by the same thread
+// (bool-mask input), so they are read with plain loads, not the read-only path.
+template <int D, bool kOwn>
 __device__ __forceinline__ void load_tile_words(const uint32_t* mrow, int kt, int W, int N, bool vec,
                                                 uint32_t (&mw)[ChainCfg<D>::kWords]) {
   using C = ChainCfg<D>;
   const int w0 = kt * C::kWords;
   if (vec) {
     if constexpr (C::kWords == 4) {
-      const uint4 v = __ldg(reinterpret_cast<const uint4*>(mrow + w0));
+      const uint4 v = kOwn ? ld_global_v4(mrow + w0) : __ldg(reinterpret_cast<const uint4*>(mrow + w0));
       mw[0] = v.x;
       mw[1] = v.y;
       mw[2] = v.z;
       mw[3] = v.w;
     } else {
-      const uint2 v = __ldg(reinterpret_cast<const uint2*>(mrow + w0));
+      const uint2 v = kOwn ? ld_global_v2(mrow + w0) : __ldg(reinterpret_cast<const uint2*>(mrow + w0));
       mw[0] = v.x;
       mw[1] = v.y;
     }
   } else {
 #pragma unroll
-    for (int w = 0; w < C::kWords; ++w) mw[w] = (w0 + w < W) ? __ldg(mrow + w0 + w) : 0u;
+    for (int w = 0; w < C::kWords; ++w)
+      mw[w] = (w0 + w < W) ? (kOwn ? ld_global_u32(mrow + w0 + w) : __ldg(mrow + w0 + w)) : 0u;
   }
   if (N - kt * C::kBN < C::kBN) {
 #pragma unroll
@@ -281,14 +286,19 @@ __device__ __forceinline__ int next_live(const uint32_t* bits, int& w, uint32_t&
   return w * 32 + b;
 }
 
-template <int D, bool BF16>
+// kBoolIn: the mask arrives as bool bytes (`bmask`, [BH, N, N]) instead of
+// packed words; the softmax warps pack each item's rows into `pk` while they
+// scan them (pk then holds exactly what the mask packer writes) and the tile
+// loop reads its words back from there.  `mask` is unused then.
+template <int D, bool BF16, bool kBoolIn>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_chain_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
                           uint16_t* __restrict__ out, const uint32_t* __restrict__ mask,
+                          const uint8_t* __restrict__ bmask, uint32_t* pk,
                           const uint32_t* __restrict__ occ, float* __restrict__ lse, int N, int BH, int W,
-                          int KT, int total_items, int vec, int o_wide, int head_major, float scale_log2,
-                          uint32_t* err_word,
+                          int KT, int total_items, int vec, int o_wide, int head_major, int pf_early,
+                          float scale_log2, uint32_t* err_word,
                           uint64_t timeout_ns) {
   using C = ChainCfg<D>;
   constexpr int kBN = C::kBN;
@@ -678,13 +688,16 @@ __global__ void __launch_bounds__(kThreads, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&bar));
     };
+    // Packed words of the tile loop: the caller's, or (bool input) this
+    // kernel's own, written by the scan of the item.
+    const uint32_t* words = kBoolIn ? pk : mask;
     auto row_ptr = [&](const Item& it) {
-      return mask + (static_cast<int64_t>(it.bh) * N + it.q0 + r) * W;
+      return words + (static_cast<int64_t>(it.bh) * N + it.q0 + r) * W;
     };
     // Mask words of key tile kt for this thread's row of `it` (0 for padding rows).
     auto fetch_words = [&](const Item& it, int kt, uint32_t (&mw)[kWords]) {
       if (r < it.rows_valid) {
-        load_tile_words<D>(row_ptr(it), kt, W, N, vec != 0, mw);
+        load_tile_words<D, kBoolIn>(row_ptr(it), kt, W, N, vec != 0, mw);
       } else {
 #pragma unroll
         for (int w = 0; w < kWords; ++w) mw[w] = 0u;
@@ -732,6 +745,72 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0 && x != 0u) atomicOr(&cc.scan_bits[j % kSlots][k], x);
       }
     };
+    // Bool input: this thread's bool row of `it` into L2 (N bytes, a hint:
+    // no registers, nothing to wait for).
+    auto prefetch_bool_row = [&](const Item& it) {
+      if (r < it.rows_valid)
+        bulk_prefetch_l2(bmask + (static_cast<int64_t>(it.bh) * N + it.q0 + r) * N, static_cast<uint32_t>(N));
+    };
+    // Bool input: packs this thread's bool row of `it` into its packed row
+    // (32 bytes -> one word, N % 32 == 0) and ORs live-tile bits into item
+    // j's scan_bits like scan_post.  Rows of 0/1 bytes (what torch writes
+    // for bool) take the multiply packing; a batch holding any other byte
+    // value is packed with the exact any-non-zero rule instead.
+    auto scan_pack = [&](const Item& it, int j) {
+      const bool row_ok = r < it.rows_valid;
+      const int64_t row = static_cast<int64_t>(it.bh) * N + it.q0 + r;
+      const uint4* brow = reinterpret_cast<const uint4*>(bmask + row * N);
+      uint32_t* prow = pk + row * W;
+      const int nw = (KT + 31) >> 5;
+      for (int k = 0; k < nw; ++k) {
+        uint32_t bits = 0u;
+        if (row_ok) {
+          const int w_lo = k * 32 * kWords;  // a multiple of 64 words
+          const int w_hi = min(W, w_lo + 32 * kWords);
+          for (int wb = w_lo; wb < w_hi; wb += kPackBatch) {
+            uint4 v[2 * kPackBatch];
+#pragma unroll
+            for (int u = 0; u < kPackBatch; ++u) {
+              const bool in = wb + u < w_hi;
+              v[2 * u] = in ? __ldcs(brow + 2 * (wb + u)) : make_uint4(0u, 0u, 0u, 0u);
+              v[2 * u + 1] = in ? __ldcs(brow + 2 * (wb + u) + 1) : make_uint4(0u, 0u, 0u, 0u);
+            }
+            bool all01 = true;
+#pragma unroll
+            for (int u = 0; u < kPackBatch; ++u) all01 = all01 && bytes_are_01(v[2 * u], v[2 * u + 1]);
+            uint32_t wd[kPackBatch];
+            if (all01) {
+#pragma unroll
+              for (int u = 0; u < kPackBatch; ++u) wd[u] = pack32_01(v[2 * u], v[2 * u + 1]);
+            } else {
+#pragma unroll
+              for (int u = 0; u < kPackBatch; ++u) wd[u] = pack32_any(v[2 * u], v[2 * u + 1]);
+            }
+            if (vec && wb + kPackBatch <= w_hi) {
+#pragma unroll
+              for (int u = 0; u < kPackBatch; u += 4)
+                *reinterpret_cast<uint4*>(prow + wb + u) = make_uint4(wd[u], wd[u + 1], wd[u + 2], wd[u + 3]);
+            } else {
+#pragma unroll
+              for (int u = 0; u < kPackBatch; ++u)
+                if (wb + u < w_hi) prow[wb + u] = wd[u];
+            }
+#pragma unroll
+            for (int u = 0; u < kPackBatch; ++u)
+              if (wd[u] != 0u) bits |= 1u << ((wb + u) / kWords - 32 * k);
+          }
+        }
+        const uint32_t x = __reduce_or_sync(0xffffffffu, bits);
+        if (lane == 0 && x != 0u) atomicOr(&cc.scan_bits[j % kSlots][k], x);
+      }
+    };
+    auto scan_item = [&](const Item& it, int j) {
+      if constexpr (kBoolIn) {
+        scan_pack(it, j);
+      } else {
+        scan_post(it, j);
+      }
+    };
     // Warp 0 of the WG, after a WG barrier: moves item j's scanned bits (lane
     // k: word k) into its slot's live bits, counts them and publishes them.
     auto publish = [&](int j) {
@@ -771,9 +850,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     // mask rows are prefetched into L1 first, so both rows are fetched from
     // HBM at once, and the first list is published before the second is built.
     const int n_pre = n_items < 2 ? n_items : 2;
-    if (n_pre > 1 && occ == nullptr) prefetch_rows_l1(item_of(chain_item(c, 1), BH, QT, N, head_major));
+    if constexpr (kBoolIn) {
+      for (int j = 0; j < n_pre; ++j) prefetch_bool_row(item_of(chain_item(c, j), BH, QT, N, head_major));
+    } else {
+      if (n_pre > 1 && occ == nullptr) prefetch_rows_l1(item_of(chain_item(c, 1), BH, QT, N, head_major));
+    }
     for (int j = 0; j < n_pre; ++j) {
-      if (occ == nullptr) scan_post(item_of(chain_item(c, j), BH, QT, N, head_major), j);
+      if (occ == nullptr) scan_item(item_of(chain_item(c, j), BH, QT, N, head_major), j);
       named_bar_sync(bar_id, 128);
       if (wq == 0) publish(j);
     }
@@ -786,6 +869,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&cc.sched_full[slot]), (i / kSlots) & 1,
                                                               abort_flag, timeout_ns));
       const uint32_t n = ok ? cc.n_live[slot] : 0u;
+      // Bool input: item i+2's rows head for L2 an item before their scan
+      // (at the item's last tile instead when the rows of a round of items
+      // would not fit in L2 together).
+      if constexpr (kBoolIn) {
+        if (pf_early && i + 2 < n_items) prefetch_bool_row(item_of(chain_item(c, i + 2), BH, QT, N, head_major));
+      }
       // Walk over the item's live bits (word lw, bits above the current tile lx).
       int lw = 0;
       uint32_t lx = cc.live_bits[slot][0];
@@ -798,6 +887,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // At the last tile, look up the next item's first live tile (its
         // list was published an item ago) so its mask words can be fetched early.
         int next_kt = -1;
+        if constexpr (kBoolIn) {
+          if (!pf_early && t + 1 == n && i + 2 < n_items)
+            prefetch_bool_row(item_of(chain_item(c, i + 2), BH, QT, N, head_major));
+        }
         if (t + 1 == n && i + 1 < n_items) {
           const int slot2 = (i + 1) % kSlots;
           if (__all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&cc.sched_full[slot2]), ((i + 1) / kSlots) & 1,
@@ -913,8 +1006,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const Item itn = item_of(chain_item(c, do_scan ? i + 2 : i), BH, QT, N, head_major);
       // D = 128 loads short rows (up to kEpiGroups 16-byte groups) outright
       // below, before it writes O.
-      const bool scan_regs = !C::kStageO && vec && G4 <= kEpiGroups;
-      if (do_scan && occ == nullptr && !scan_regs) prefetch_rows_l1(itn);
+      const bool scan_regs = !kBoolIn && !C::kStageO && vec && G4 <= kEpiGroups;
+      if (!kBoolIn && do_scan && occ == nullptr && !scan_regs) prefetch_rows_l1(itn);
       const float inv = (l_out > 0.f) ? (1.f / l_out) : 0.f;
       const bool o_ready = ok && n > 0 && wait_all(cc.pv_done, (g - 1) & 1);
       if (n > 0 && !o_ready) ok = false;
@@ -937,7 +1030,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int e = 0; e < 16; ++e)
             h[half * 16 + e] = pack2<BF16>(__uint_as_float(u[2 * e]) * inv, __uint_as_float(u[2 * e + 1]) * inv);
         }
-        if (do_scan && occ == nullptr) scan_post(itn, i + 2);
+        if (do_scan && occ == nullptr) scan_item(itn, i + 2);
         // The previous item's O store must have finished reading the staging tile.
         if (r == 0) bulk_wait_group_read0();
         named_bar_sync(bar_id, 128);
@@ -1002,7 +1095,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint32_t x = __reduce_or_sync(0xffffffffu, bits);
             if (lane == 0 && x != 0u) atomicOr(&cc.scan_bits[(i + 2) % kSlots][0], x);
           } else {
-            scan_post(itn, i + 2);
+            scan_item(itn, i + 2);
           }
         }
         named_bar_sync(bar_id, 128);
@@ -1025,7 +1118,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ---------------------------------------------------------------- host side
 
-template <int D, bool BF16>
+template <int D, bool BF16, bool kBoolIn>
 int launch(const AttnParams& p, const char** msg) {
   using C = ChainCfg<D>;
   constexpr size_t kSmemBytes = smem_bytes<D>();
@@ -1040,15 +1133,18 @@ int launch(const AttnParams& p, const char** msg) {
     return kErrArg;
   }
   CUtensorMap mq, mk, mv, mo;
-  if (!make_tensor_map_3d(&mq, p.q, p.dtype, D, BH, N, kBM) || !make_tensor_map_3d(&mk, p.k, p.dtype, D, BH, N, C::kBN) ||
-      !make_tensor_map_3d(&mv, p.v, p.dtype, D, BH, N, C::kBN) || !make_tensor_map_3d(&mo, p.out, p.dtype, D, BH, N, kBM)) {
-    *msg = "attention: cuTensorMapEncodeTiled failed (pointer alignment or driver entry point)";
+  CUresult rc = make_tensor_map_3d(&mq, p.q, p.dtype, D, BH, N, kBM);
+  if (rc == CUDA_SUCCESS) rc = make_tensor_map_3d(&mk, p.k, p.dtype, D, BH, N, C::kBN);
+  if (rc == CUDA_SUCCESS) rc = make_tensor_map_3d(&mv, p.v, p.dtype, D, BH, N, C::kBN);
+  if (rc == CUDA_SUCCESS) rc = make_tensor_map_3d(&mo, p.out, p.dtype, D, BH, N, kBM);
+  if (rc != CUDA_SUCCESS) {
+    *msg = tensor_map_error("attention", rc);
     return kErrCuda;
   }
   DeviceProps dp;
   if (!device_props(&dp, msg)) return kErrCuda;
   static std::atomic<bool> smem_set[kMaxDevices] = {};
-  auto kern = attn_fwd_chain_kernel<D, BF16>;
+  auto kern = attn_fwd_chain_kernel<D, BF16, kBoolIn>;
   {
     cudaError_t e = ensure_smem_limit(kern, kSmemBytes, dp.device, smem_set);
     if (e != cudaSuccess) {
@@ -1056,18 +1152,24 @@ int launch(const AttnParams& p, const char** msg) {
       return kErrLaunch;
     }
   }
-  const int vec = (W % 4 == 0 && (reinterpret_cast<uintptr_t>(p.mask) & 15u) == 0) ? 1 : 0;
+  // Bool input: the kernel packs into p.packed_out and reads its words back.
+  const uint32_t* words = kBoolIn ? p.packed_out : p.mask;
+  const int vec = (W % 4 == 0 && (reinterpret_cast<uintptr_t>(words) & 15u) == 0) ? 1 : 0;
   const int o_wide = (reinterpret_cast<uintptr_t>(p.out) & 31u) == 0 ? 1 : 0;  // 32-byte O stores (D = 128)
   // Head-major item order once K and V of all heads exceed half of L2.
   const int head_major = 2 * BH * N * D * 2 > dp.l2_bytes / 2 ? 1 : 0;
   const int grid = static_cast<int>(total < dp.sms ? total : dp.sms);
   // The occupancy map describes 128-key tiles: only the D = 64 kernel uses it.
-  const uint32_t* occ = D == 64 ? p.occ : nullptr;
+  const uint32_t* occ = (D == 64 && !kBoolIn) ? p.occ : nullptr;
+  // Bool input: item i+2's bool rows are prefetched into L2 when item i
+  // starts if two rounds of items' rows (2 chains per CTA) take at most 48
+  // MB of L2, else at item i's last tile.
+  const int pf_early = 2 * static_cast<int64_t>(grid) * 2 * kBM * N <= (int64_t{48} << 20) ? 1 : 0;
   cudaError_t e = launch_pdl(kern, static_cast<unsigned>(grid), kThreads, kSmemBytes, p.stream, mq, mk, mv, mo,
-                             static_cast<uint16_t*>(p.out), p.mask, occ, p.lse, static_cast<int>(N), static_cast<int>(BH), static_cast<int>(W),
-                             static_cast<int>(KT), static_cast<int>(total), vec, o_wide, head_major,
-                             p.scale * kLog2e, p.err_word,
-                             p.timeout_ns);
+                             static_cast<uint16_t*>(p.out), kBoolIn ? nullptr : p.mask, kBoolIn ? p.bmask : nullptr,
+                             kBoolIn ? p.packed_out : nullptr, occ, p.lse, static_cast<int>(N), static_cast<int>(BH),
+                             static_cast<int>(W), static_cast<int>(KT), static_cast<int>(total), vec, o_wide,
+                             head_major, pf_early, p.scale * kLog2e, p.err_word, p.timeout_ns);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) {
     static thread_local char buf[256];
@@ -1088,8 +1190,12 @@ bool chain_supported(const AttnParams& p) {
 }
 
 int launch_attn_fwd_chain(const AttnParams& p, const char** msg) {
-  if (p.D == 128) return p.dtype == 1 ? launch<128, true>(p, msg) : launch<128, false>(p, msg);
-  return p.dtype == 1 ? launch<64, true>(p, msg) : launch<64, false>(p, msg);
+  if (p.bmask != nullptr) {
+    if (p.D == 128) return p.dtype == 1 ? launch<128, true, true>(p, msg) : launch<128, false, true>(p, msg);
+    return p.dtype == 1 ? launch<64, true, true>(p, msg) : launch<64, false, true>(p, msg);
+  }
+  if (p.D == 128) return p.dtype == 1 ? launch<128, true, false>(p, msg) : launch<128, false, false>(p, msg);
+  return p.dtype == 1 ? launch<64, true, false>(p, msg) : launch<64, false, false>(p, msg);
 }
 
 }  // namespace sma

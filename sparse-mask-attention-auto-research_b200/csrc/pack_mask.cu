@@ -16,23 +16,12 @@
 // thread with all eight 16-byte loads issued before any use.
 // General path: one thread per output word with byte loads (any N, any
 // alignment).
+#include "mask_bits.cuh"
 #include "sma_internal.h"
 #include "sma_ptx.cuh"
 
 namespace sma {
 namespace {
-
-// 4 mask bytes -> 4 bits (byte k -> bit k), treating any non-zero byte as set.
-__device__ __forceinline__ uint32_t pack4(uint32_t x) {
-  // High bit of each byte := byte != 0 (no carries cross byte lanes).
-  uint32_t hi = (((x & 0x7F7F7F7Fu) + 0x7F7F7F7Fu) | x) & 0x80808080u;
-  // Gather the four high bits into bits 28..31 with one multiply.
-  return (hi * 0x00204081u) >> 28;
-}
-
-__device__ __forceinline__ uint32_t pack16(uint4 v) {
-  return pack4(v.x) | (pack4(v.y) << 4) | (pack4(v.z) << 8) | (pack4(v.w) << 12);
-}
 
 constexpr int kPackThreads = 256;
 constexpr int kPackRounds = 4;
@@ -59,7 +48,7 @@ __global__ void __launch_bounds__(kPackThreads) pack_mask_aligned_kernel(
 #pragma unroll
   for (int r = 0; r < kPackRounds; ++r) {
     const int64_t w = base + r * 32 + lane;
-    if (w < total_words) out[w] = pack16(lo[r]) | (pack16(hi[r]) << 16);
+    if (w < total_words) out[w] = pack32_any(lo[r], hi[r]);
   }
 }
 
@@ -117,7 +106,7 @@ __global__ void __launch_bounds__(kOccThreads) pack_mask_occ_kernel(
     for (int r = 0; r < kOccRounds; ++r) {
       const int w = w0 + r * kOccThreads;
       if (w < words) {
-        const uint32_t word = pack16(a[r]) | (pack16(b[r]) << 16);
+        const uint32_t word = pack32_any(a[r], b[r]);
         out[base + w] = word;
         if (word != 0u) {
           const int tile = (w % n_words) >> 2;  // four 32-column words per key tile

@@ -47,12 +47,20 @@ int fail_cuda(cudaError_t e, const char* where) {
   return sma::kErrCuda;
 }
 
-// Device address of the error word on the current device.
+// Device address of the error word on the current device.  Every entry point
+// that launches calls this first; it also makes the device's primary context
+// current on the calling thread, which the runtime otherwise binds only at the
+// thread's first runtime call that needs it, while the tensor-map encoding
+// (a driver call) needs it bound already.  A host thread whose first CUDA
+// work is a call into this library (an autograd worker, say) would otherwise
+// fail there.
 int error_word(uint32_t** out) {
   int dev = -1;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
   if (dev < 0 || dev >= kMaxDevices) return fail(sma::kErrCuda, "device index out of range");
+  e = cudaSetDevice(dev);
+  if (e != cudaSuccess) return fail_cuda(e, "cudaSetDevice");
   uint32_t* ptr = g_err_ptr[dev].load(std::memory_order_relaxed);
   if (ptr == nullptr) {
     void* p = nullptr;
@@ -113,10 +121,12 @@ int sma_pack_mask(const void* mask, void* packed, int64_t B, int64_t H, int64_t 
 
 namespace {
 
+// bool_mask != nullptr: the forward reads the bool mask itself and writes the
+// packed words to mask_packed (sma_attn_fwd_mask).
 int attn_fwd_impl(int dtype, const void* q, const void* k, const void* v, const void* mask_packed,
-                  const uint32_t* occupancy, void* out, float* lse, int64_t B, int64_t H, int64_t N, int64_t D,
-                  float scale, void* stream) {
-  NvtxRange range("sma_attn_fwd");
+                  const uint32_t* occupancy, const void* bool_mask, void* out, float* lse, int64_t B, int64_t H,
+                  int64_t N, int64_t D, float scale, void* stream) {
+  NvtxRange range(bool_mask != nullptr ? "sma_attn_fwd_mask" : "sma_attn_fwd");
   if (dtype != SMA_DTYPE_FP16 && dtype != SMA_DTYPE_BF16)
     return fail(sma::kErrDtype, "attention: unsupported dtype, need fp16 or bf16");
   if (B < 0 || H < 0 || N < 0 || D <= 0) return fail(sma::kErrArg, "attention: bad dimension");
@@ -132,6 +142,8 @@ int attn_fwd_impl(int dtype, const void* q, const void* k, const void* v, const 
     return fail(sma::kErrArg, "attention: q/k/v/out must be 16-byte aligned");
   if ((reinterpret_cast<uintptr_t>(mask_packed) & 3u) != 0 || (lse && (reinterpret_cast<uintptr_t>(lse) & 3u)))
     return fail(sma::kErrArg, "attention: mask_packed/lse must be 4-byte aligned");
+  if (bool_mask != nullptr && (N % 32 != 0 || !aligned16(bool_mask) || !aligned16(mask_packed)))
+    return fail(sma::kErrArg, "attention: the bool-mask forward needs N % 32 == 0 and 16-byte aligned mask / mask_packed");
   uint32_t* err = nullptr;
   int rc = error_word(&err);
   if (rc != sma::kOk) return rc;
@@ -142,6 +154,8 @@ int attn_fwd_impl(int dtype, const void* q, const void* k, const void* v, const 
   p.v = v;
   p.mask = static_cast<const uint32_t*>(mask_packed);
   p.occ = occupancy;
+  p.bmask = static_cast<const uint8_t*>(bool_mask);
+  p.packed_out = bool_mask != nullptr ? static_cast<uint32_t*>(const_cast<void*>(mask_packed)) : nullptr;
   p.out = out;
   p.lse = lse;
   p.B = B;
@@ -163,7 +177,13 @@ extern "C" {
 
 int sma_attn_fwd(int dtype, const void* q, const void* k, const void* v, const void* mask_packed, void* out,
                  float* lse, int64_t B, int64_t H, int64_t N, int64_t D, float scale, void* stream) {
-  return attn_fwd_impl(dtype, q, k, v, mask_packed, nullptr, out, lse, B, H, N, D, scale, stream);
+  return attn_fwd_impl(dtype, q, k, v, mask_packed, nullptr, nullptr, out, lse, B, H, N, D, scale, stream);
+}
+
+int sma_attn_fwd_mask(int dtype, const void* q, const void* k, const void* v, const void* mask, void* mask_packed,
+                      void* out, float* lse, int64_t B, int64_t H, int64_t N, int64_t D, float scale, void* stream) {
+  if (mask == nullptr && B > 0 && H > 0 && N > 0) return fail(sma::kErrArg, "attention: null mask");
+  return attn_fwd_impl(dtype, q, k, v, mask_packed, nullptr, mask, out, lse, B, H, N, D, scale, stream);
 }
 
 int sma_pack_mask_occupancy(const void* mask, void* packed, void* occupancy, int64_t B, int64_t H, int64_t N,
@@ -186,8 +206,8 @@ int sma_attn_fwd_occupancy(int dtype, const void* q, const void* k, const void* 
   if (occupancy == nullptr) return fail(sma::kErrArg, "attention: null occupancy map");
   if ((reinterpret_cast<uintptr_t>(occupancy) & 3u) != 0)
     return fail(sma::kErrArg, "attention: occupancy map must be 4-byte aligned");
-  return attn_fwd_impl(dtype, q, k, v, mask_packed, static_cast<const uint32_t*>(occupancy), out, lse, B, H, N, D,
-                       scale, stream);
+  return attn_fwd_impl(dtype, q, k, v, mask_packed, static_cast<const uint32_t*>(occupancy), nullptr, out, lse, B, H,
+                       N, D, scale, stream);
 }
 
 int sma_attn_bwd(int dtype, const void* q, const void* k, const void* v, const void* out, const void* dout,

@@ -32,6 +32,11 @@ struct AttnParams {
   int64_t B, H, N, D;
   float scale;
   const uint32_t* occ;        // [B*H, ceil(N/128), 2] live key-tile bits per query tile, or nullptr
+  // Bool-mask input instead of `mask`: [B, H, N, N] bytes (non-zero = attend),
+  // N % 32 == 0, 16-byte aligned; the kernel writes the packed words to
+  // packed_out ([B, H, N, N/32], 16-byte aligned) and reads them back.
+  const uint8_t* bmask;
+  uint32_t* packed_out;
   uint32_t* err_word;         // device word the kernel ORs error bits into
   uint64_t timeout_ns;        // bound on every device-side wait
   cudaStream_t stream;
@@ -80,11 +85,14 @@ int launch_attn_bwd(const BwdParams& p, const char** msg);
 
 // TMA map of the [BH, N, D] view of a contiguous [B, H, N, D] fp16/bf16
 // tensor: boxes of 64 head dims (one 128-byte swizzle span) by `rows` rows,
-// 128-byte swizzle (tma_map.cu).
-bool make_tensor_map_3d(CUtensorMap* m, const void* ptr, int dtype, int64_t D, int64_t BH, int64_t N, int rows);
+// 128-byte swizzle (tma_map.cu).  Returns the driver's status
+// (CUDA_ERROR_NOT_FOUND when the entry point is missing).
+CUresult make_tensor_map_3d(CUtensorMap* m, const void* ptr, int dtype, int64_t D, int64_t BH, int64_t N, int rows);
 // The same view of a contiguous FP32 [BH, N, D] tensor: boxes of 32 elements
 // (128 bytes) by `rows` rows, 128-byte swizzle (tma_map.cu).
-bool make_tensor_map_3d_f32(CUtensorMap* m, const void* ptr, int64_t D, int64_t BH, int64_t N, int rows);
+CUresult make_tensor_map_3d_f32(CUtensorMap* m, const void* ptr, int64_t D, int64_t BH, int64_t N, int rows);
+// Message for a failed tensor-map encode: `what` and the driver status.
+const char* tensor_map_error(const char* what, CUresult rc);
 
 // Devices the per-device caches of the launchers cover.
 constexpr int kMaxDevices = 64;

@@ -3,6 +3,7 @@
 // (cudaGetDriverEntryPoint), so the library does not link libcuda.
 #include <cudaTypedefs.h>
 
+#include <cstdio>
 #include <mutex>
 
 #include "sma_internal.h"
@@ -55,9 +56,9 @@ bool device_props(DeviceProps* out, const char** msg) {
   return true;
 }
 
-bool make_tensor_map_3d(CUtensorMap* m, const void* ptr, int dtype, int64_t D, int64_t BH, int64_t N, int rows) {
+CUresult make_tensor_map_3d(CUtensorMap* m, const void* ptr, int dtype, int64_t D, int64_t BH, int64_t N, int rows) {
   auto fn = encode_fn();
-  if (fn == nullptr) return false;
+  if (fn == nullptr) return CUDA_ERROR_NOT_FOUND;
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(BH)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(D * 2), static_cast<cuuint64_t>(N * D * 2)};
   cuuint32_t box[3] = {64u, static_cast<cuuint32_t>(rows), 1u};
@@ -65,21 +66,28 @@ bool make_tensor_map_3d(CUtensorMap* m, const void* ptr, int dtype, int64_t D, i
   return fn(m, dtype == 1 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
             const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
 }
 
 // FP32 [BH][N][D] tensor, boxes of 32 elements (128 bytes, 128-byte swizzle)
 // by `rows` rows.
-bool make_tensor_map_3d_f32(CUtensorMap* m, const void* ptr, int64_t D, int64_t BH, int64_t N, int rows) {
+CUresult make_tensor_map_3d_f32(CUtensorMap* m, const void* ptr, int64_t D, int64_t BH, int64_t N, int rows) {
   auto fn = encode_fn();
-  if (fn == nullptr) return false;
+  if (fn == nullptr) return CUDA_ERROR_NOT_FOUND;
   cuuint64_t dims[3] = {static_cast<cuuint64_t>(D), static_cast<cuuint64_t>(N), static_cast<cuuint64_t>(BH)};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(D * 4), static_cast<cuuint64_t>(N * D * 4)};
   cuuint32_t box[3] = {32u, static_cast<cuuint32_t>(rows), 1u};
   cuuint32_t estr[3] = {1u, 1u, 1u};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(ptr), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+const char* tensor_map_error(const char* what, CUresult rc) {
+  static thread_local char buf[160];
+  snprintf(buf, sizeof(buf), "%s: cuTensorMapEncodeTiled failed (CUresult %d; pointer alignment, shape, or no driver entry point)",
+           what, static_cast<int>(rc));
+  return buf;
 }
 
 }  // namespace sma

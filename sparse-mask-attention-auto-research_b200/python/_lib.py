@@ -36,6 +36,10 @@ SIGNATURES = {
         ctypes.c_int,
         [ctypes.c_int, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, ctypes.c_float, _vp],
     ),
+    "sma_attn_fwd_mask": (
+        ctypes.c_int,
+        [ctypes.c_int, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, ctypes.c_float, _vp],
+    ),
     "sma_pack_mask_occupancy": (ctypes.c_int, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "sma_attn_fwd_occupancy": (
         ctypes.c_int,

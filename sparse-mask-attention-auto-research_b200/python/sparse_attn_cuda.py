@@ -13,7 +13,12 @@ mask geometry), since the raw kernels would otherwise read out of bounds.
 ``lse`` may be None when ``is_training`` is False (the reference's
 ``sparse_attention_func`` passes None there and fails to bind it).
 
-Beyond the reference: ``pack_mask_occupancy(mask)`` packs and also returns
+Beyond the reference: ``forward_mask(q, k, v, mask, mask_packed, out, lse,
+scale, is_training)`` is the pack + forward pair in one launch: the attention
+kernel reads the bool mask, writes the packed words into ``mask_packed`` (for
+the backward) and computes ``out`` / ``lse`` exactly as ``forward`` does on
+them.  ``forward_mask_supported(mask)`` says when it applies.
+``pack_mask_occupancy(mask)`` packs and also returns
 the per-(batch*head, 128-row query tile) map of live 128-key tiles, and
 ``forward(..., occupancy=map)`` lets the kernel skip dead tiles from that
 map instead of scanning the packed rows (same results).
@@ -38,9 +43,8 @@ def _require(cond, msg):
         raise RuntimeError(msg)
 
 
-def forward(q, k, v, mask_packed, out, lse, scale, is_training, occupancy=None):
-    """Sparse attention forward (reference csrc/binding.cpp:9-47).  The optional
-    ``occupancy`` is the map returned by pack_mask_occupancy for this mask."""
+def _check_forward_args(q, k, v, mask_packed, out, lse, is_training):
+    """The reference binding's checks plus shape / contiguity; returns the lse pointer."""
     _require(q.is_cuda, "q must be CUDA tensor")
     _require(q.dim() == 4, "q must be 4D")
     _require(q.dtype in _DTYPES, "Unsupported dtype, need BF16 or FP16")
@@ -59,14 +63,51 @@ def forward(q, k, v, mask_packed, out, lse, scale, is_training, occupancy=None):
         f"mask_packed must have shape {(B, H, N, n_words)}, got {tuple(mask_packed.shape)}",
     )
     _require(mask_packed.is_contiguous(), "mask_packed must be contiguous")
-    lse_ptr = None
-    if is_training:
-        _require(lse is not None, "lse is required when is_training is true")
-        _require(lse.device == q.device, "lse must be on the same device as q")
-        _require(lse.dtype == torch.float32, "lse must be float32")
-        _require(tuple(lse.shape) == (B, H, N), f"lse must have shape {(B, H, N)}")
-        _require(lse.is_contiguous(), "lse must be contiguous")
-        lse_ptr = lse.data_ptr()
+    if not is_training:
+        return None
+    _require(lse is not None, "lse is required when is_training is true")
+    _require(lse.device == q.device, "lse must be on the same device as q")
+    _require(lse.dtype == torch.float32, "lse must be float32")
+    _require(tuple(lse.shape) == (B, H, N), f"lse must have shape {(B, H, N)}")
+    _require(lse.is_contiguous(), "lse must be contiguous")
+    return lse.data_ptr()
+
+
+def forward_mask_supported(mask):
+    """True when forward_mask takes this bool mask: N % 32 == 0, contiguous,
+    16-byte aligned."""
+    N = mask.shape[-1]
+    return N % 32 == 0 and mask.is_contiguous() and mask.data_ptr() % 16 == 0
+
+
+def forward_mask(q, k, v, mask, mask_packed, out, lse, scale, is_training):
+    """pack_mask(mask) into ``mask_packed`` and forward(q, k, v, mask_packed,
+    out, lse, scale, is_training) in one launch: the attention kernel reads
+    the bool mask itself.  ``mask_packed`` ([B, H, N, N/32] int32, 16-byte
+    aligned) receives exactly what pack_mask returns; out and lse are those
+    forward writes.  Needs forward_mask_supported(mask)."""
+    lse_ptr = _check_forward_args(q, k, v, mask_packed, out, lse, is_training)
+    B, H, N, D = q.shape
+    _require(mask.device == q.device, "mask must be on the same device as q")
+    _require(mask.dtype == torch.bool, "mask must be a bool tensor")
+    _require(tuple(mask.shape) == (B, H, N, N), f"mask must have shape {(B, H, N, N)}, got {tuple(mask.shape)}")
+    _require(forward_mask_supported(mask), "forward_mask needs N % 32 == 0 and a contiguous 16-byte aligned mask")
+    _require(mask_packed.data_ptr() % 16 == 0, "mask_packed must be 16-byte aligned")
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        _lib.check(
+            lib.sma_attn_fwd_mask(
+                _DTYPES[q.dtype], q.data_ptr(), k.data_ptr(), v.data_ptr(), mask.data_ptr(), mask_packed.data_ptr(),
+                out.data_ptr(), lse_ptr, B, H, N, D, float(scale), _stream_ptr(q.device),
+            )
+        )
+
+
+def forward(q, k, v, mask_packed, out, lse, scale, is_training, occupancy=None):
+    """Sparse attention forward (reference csrc/binding.cpp:9-47).  The optional
+    ``occupancy`` is the map returned by pack_mask_occupancy for this mask."""
+    lse_ptr = _check_forward_args(q, k, v, mask_packed, out, lse, is_training)
+    B, H, N, D = q.shape
     lib = _lib.load()
     if occupancy is not None:
         q_tiles = (N + 127) // 128
