@@ -1009,31 +1009,40 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool scan_regs = !kBoolIn && !C::kStageO && vec && G4 <= kEpiGroups;
       if (!kBoolIn && do_scan && occ == nullptr && !scan_regs) prefetch_rows_l1(itn);
       const float inv = (l_out > 0.f) ? (1.f / l_out) : 0.f;
-      const bool o_ready = ok && n > 0 && wait_all(cc.pv_done, (g - 1) & 1);
-      if (n > 0 && !o_ready) ok = false;
       const float lse_row = (l_run > 0.f) ? (m_run + log2f(l_run)) * kLn2 : -FLT_MAX;
+      // The last PV of the item (O complete); a warp-wide wait.
+      auto wait_o = [&]() -> bool {
+        const bool ready = ok && n > 0 && wait_all(cc.pv_done, (g - 1) & 1);
+        if (n > 0 && !ready) ok = false;
+        return ready;
+      };
       if constexpr (C::kStageO) {
-        // O of the item, normalised and packed to 16-bit pairs (32 words per
-        // row), through the staging tile and one TMA store.
-        uint32_t h[32];
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          uint32_t u[32];
-          if (o_ready) {
-            tmem_ld32(t_lane + kOCol + half * 32, u);
-            tmem_wait_ld();
-          } else {
-#pragma unroll
-            for (int e = 0; e < 32; ++e) u[e] = 0u;
-          }
-#pragma unroll
-          for (int e = 0; e < 16; ++e)
-            h[half * 16 + e] = pack2<BF16>(__uint_as_float(u[2 * e]) * inv, __uint_as_float(u[2 * e + 1]) * inv);
-        }
+        // The work that does not need O goes first, under the last PV's
+        // latency: the scan of item i+2, the barrier that also frees the
+        // staging tile (the previous item's O store has read it), and the
+        // publication of item i+2's list.
         if (do_scan && occ == nullptr) scan_item(itn, i + 2);
-        // The previous item's O store must have finished reading the staging tile.
         if (r == 0) bulk_wait_group_read0();
         named_bar_sync(bar_id, 128);
+        if (wq == 0 && do_scan) publish(i + 2);
+        // O of the item, normalised and packed to 16-bit pairs (32 words per
+        // row), through the staging tile and one TMA store.
+        const bool o_ready = wait_o();
+        uint32_t u0[32], u1[32];
+        if (o_ready) {
+          tmem_ld32(t_lane + kOCol, u0);
+          tmem_ld32(t_lane + kOCol + 32, u1);
+          tmem_wait_ld();
+        } else {
+#pragma unroll
+          for (int e = 0; e < 32; ++e) u0[e] = u1[e] = 0u;
+        }
+        uint32_t h[32];
+#pragma unroll
+        for (int e = 0; e < 16; ++e) {
+          h[e] = pack2<BF16>(__uint_as_float(u0[2 * e]) * inv, __uint_as_float(u0[2 * e + 1]) * inv);
+          h[16 + e] = pack2<BF16>(__uint_as_float(u1[2 * e]) * inv, __uint_as_float(u1[2 * e + 1]) * inv);
+        }
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           const int chunk = q ^ (r & 7);  // 128-byte swizzle of the O tensor map
@@ -1047,8 +1056,8 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_store_3d(&tm_o, sO, 0, it.q0, it.bh);
           bulk_commit_group();
         }
-        if (wq == 0 && do_scan) publish(i + 2);
       } else {
+        const bool o_ready = wait_o();
         // The scan loads of item i+2 go first and land while O is written.
         uint4 sv[kEpiGroups];
         const bool load_sv = scan_regs && do_scan && occ == nullptr && r < itn.rows_valid;
