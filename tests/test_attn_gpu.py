@@ -242,3 +242,28 @@ def test_items_without_live_tiles_between_live_items(name, empty_rounds):
     ref_out, ref_lse = oracle.attention_parallel(qf, kf, vf, mf.astype(bool), 1 / math.sqrt(D), with_lse=True)
     check_against(out.reshape(BH, N, D)[heads], lse.reshape(BH, N)[heads], torch.from_numpy(ref_out),
                   torch.from_numpy(ref_lse), torch.from_numpy(mf.astype(bool)), q.dtype)
+
+
+@pytest.mark.parametrize("H,N,D,dtype", [(44, 512, 64, torch.float16), (200, 128, 128, torch.bfloat16),
+                                         (40, 480, 64, torch.bfloat16), (56, 384, 128, torch.float16)])
+def test_partial_last_round(H, N, D, dtype):
+    """Shapes whose last round has more items than SMs but fewer than
+    chains (some SMs run two items in it, others one), with ragged N, fully
+    masked rows, heads whose middle key tiles are dead, a fully masked head
+    and a row whose only key is the last one: against the oracle, and
+    bit-identical across runs."""
+    g = torch.Generator(device=DEV).manual_seed(H * N + D)
+    q, k, v = (torch.randn(1, H, N, D, generator=g, device=DEV).to(dtype) for _ in range(3))
+    m = torch.rand(1, H, N, N, generator=g, device=DEV) < 0.2
+    m[:, ::3, :, 64:200] = False          # dead key tiles in every third head
+    m[:, 1, :, :] = False                 # a fully masked head
+    m[:, :, 7, :] = False                 # a fully masked row in every head
+    m[:, 2, 100, :] = False
+    m[:, 2, 100, N - 1] = True            # a row whose only key is the last one
+    o1, l1 = run_fwd(q, k, v, m)
+    o2, l2 = run_fwd(q, k, v, m)
+    assert torch.equal(o1, o2) and torch.equal(l1, l2)
+    ref_out = oracle.attention(*(x.float().cpu().numpy() for x in (q, k, v)), m.cpu().numpy(), 1 / math.sqrt(D))
+    ref_lse = oracle.lse(q.float().cpu().numpy(), k.float().cpu().numpy(), m.cpu().numpy(), 1 / math.sqrt(D))
+    check_against(o1, l1, torch.from_numpy(ref_out), torch.from_numpy(ref_lse), m, dtype,
+                  name=f"partial last round H{H} N{N} D{D} {str(dtype)[6:]}")
