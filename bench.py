@@ -20,8 +20,9 @@ GPUs every rank runs its own c1 batch (weak scaling, `value`).  Every line
 also carries `strong_c5`: the large-batch workload c5 (B256 H16 N512 D64)
 split by batch*head over the N ranks, max-over-ranks step time, and its
 efficiency against one GPU running all of c5 in the same run.  The one-GPU
-line adds `configs` (c1..c5 step, attention and roofline figures) and
-`backward` (the backward kernel on c1).
+line adds `configs` (c1..c5 step, attention and roofline figures),
+`backward` (the backward kernel on c1) and `sweep` (the reference's own
+performance sweep, run.py:483-540: N from 64 to 16384 and B from 1 to 64).
 
 Prints ONE JSON line on rank 0.  --impl reference times the reference's own
 CPU implementation of the path (its torch masked-softmax attention,
@@ -291,8 +292,9 @@ def attn_roofline(name, lb, lh, N, D, m, attn_ms_mean, peaks):
 
 
 def measure_forward(name, dev, flush, steps, seed, heads=None, with_split=True):
-    """p50 / mean step and split times of the forward on workload `name`
-    (optionally a slice of its flattened batch*head range)."""
+    """p50 / mean step and split times of the forward on workload `name` (or
+    a workload config dict), optionally a slice of its flattened batch*head
+    range."""
     from python import workloads
 
     q, k, v, m = workloads.make_inputs(name, seed=seed, device=dev, heads=heads)
@@ -594,6 +596,7 @@ def run_ours(args):
         if world == 1:
             blocks["configs"] = configs_block(args, dev, flush, peaks, blocks["strong_c5"])
             blocks["backward"] = backward_block(args, dev, flush, peaks)
+            blocks["sweep"] = sweep_block(args, dev, flush, peaks)
 
     # ---- CPU baseline (the reference's CPU path) on rank 0 at N=1 only
     cpu_baseline = None
@@ -738,6 +741,32 @@ def configs_block(args, dev, flush, peaks, c5):
                      "mma_bound_us": rl["mma_bound_us"], "live_tile_fraction": rl["live_tile_fraction"],
                      "tile": rl["tile"], "live_tile_fraction_128x64": rl["live_tile_fraction_128x64"],
                      "steps": args.block_steps}
+        del r, q, m
+        torch.cuda.empty_cache()
+    return out
+
+
+def sweep_block(args, dev, flush, peaks):
+    """The reference's own performance sweep (run.py:483-540) on this library:
+    sequence-length scaling (B chosen by N) and batch scaling at N = 512,
+    H12 D64 fp16, prefix_random masks (python/workloads.py).  Per shape the
+    step (pack + attention) p50, dense-equivalent TFLOPS, and the attention
+    kernel's roofline fraction, under the same flush as every other block."""
+    from python import workloads
+
+    out = []
+    for label, cfg in workloads.sweep_shapes():
+        r = measure_forward(cfg, dev, flush, args.block_steps, args.seed)
+        q, m = r["q"], r["m"]
+        B, H, N, D = q.shape
+        rl = attn_roofline(label, B, H, N, D, m, r["attn_ms_mean"], peaks)
+        density = float(m.sum(dtype=torch.int64)) / m.numel()
+        out.append({"shape": label, "B": B, "H": H, "N": N, "D": D, "density": density,
+                    "step_ms_p50": r["step_ms_p50"], "attn_ms_p50": r["attn_ms_p50"],
+                    "pack_ms_p50": r["pack_ms_p50"],
+                    "tflops_dense_equiv": workloads.dense_flops(B, H, N, D) / (r["step_ms_p50"] * 1e-3) / 1e12,
+                    "seq_per_s": B / (r["step_ms_p50"] * 1e-3), "bound": rl["bound"], "frac": rl["frac"],
+                    "live_tile_fraction": rl["live_tile_fraction"], "steps": args.block_steps})
         del r, q, m
         torch.cuda.empty_cache()
     return out

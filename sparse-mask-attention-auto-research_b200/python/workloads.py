@@ -10,6 +10,11 @@ Workloads (q, k, v ~ N(0, 1); scale 1/sqrt(D); True = attend):
 
 Inputs are generated per head from a seed so that any slice of the flattened
 B*H range (a multi-GPU shard) is exactly the slice of the global tensors.
+
+The reference's performance sweep (run.py:483-540) uses a further mask,
+"prefix_random" (run.py:181-203): row i attends every key j >= i plus
+min(num_prev, i) keys j < i drawn uniformly without replacement
+(num_prev = 2048, H12 D64 fp16); sweep_shapes() lists its shapes.
 """
 
 import math
@@ -46,6 +51,26 @@ def _mask_block(cfg, nh, N, gen, device):
         m = alive & (torch.rand(nh, N, N, generator=gen, device=device) < cfg["keep"])
         m |= torch.eye(N, dtype=torch.bool, device=device)
         return m
+    if kind == "prefix_random":
+        # Keys j >= i, plus the num_prev lowest of uniform scores among j < i
+        # (all of them when i <= num_prev), one head at a time to bound memory.
+        i = torch.arange(N, device=device)
+        later = i[None, :] >= i[:, None]
+        k = min(cfg["num_prev"], N - 1)
+        if k >= N - 1:
+            return torch.ones(nh, N, N, dtype=torch.bool, device=device)
+        heads = []
+        for _ in range(nh):
+            scores = torch.rand(N, N, generator=gen, device=device)
+            scores.masked_fill_(later, float("inf"))
+            idx = torch.topk(scores, k, dim=-1, largest=False).indices
+            del scores
+            m = torch.zeros(N, N, dtype=torch.bool, device=device)
+            m.scatter_(-1, idx, True)
+            m &= ~later
+            m |= later
+            heads.append(m)
+        return torch.stack(heads)
     if kind == "causal":
         i = torch.arange(N, device=device)
         causal = i[None, :] <= i[:, None]
@@ -53,6 +78,20 @@ def _mask_block(cfg, nh, N, gen, device):
         m |= torch.eye(N, dtype=torch.bool, device=device)
         return m
     raise ValueError(kind)
+
+
+def sweep_shapes():
+    """The reference's performance sweep (run.py:497-540): sequence-length
+    scaling with B chosen by N, and batch scaling at N = 512; H12 D64 fp16,
+    prefix_random masks with num_prev 2048.  Returns (name, cfg) pairs."""
+    base = dict(H=12, D=64, dtype=torch.float16, mask="prefix_random", num_prev=2048)
+    out = []
+    for N in (64, 128, 256, 512, 1024, 2048, 4096, 8192, 16384):
+        B = 16 if N <= 1024 else 4 if N <= 4096 else 2 if N <= 8192 else 1
+        out.append((f"seq N{N} B{B}", dict(base, B=B, N=N)))
+    for B in (1, 4, 8, 16, 32, 64):
+        out.append((f"batch B{B} N512", dict(base, B=B, N=512)))
+    return out
 
 
 def make_inputs(name_or_cfg, seed=0, device="cpu", heads=None, **overrides):
