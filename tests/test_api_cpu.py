@@ -69,6 +69,32 @@ def test_mask_recipes(name):
         assert abs(m.float().mean().item() - 0.076) < 0.02
 
 
+@pytest.mark.parametrize("N,num_prev", [(64, 16), (96, 200), (40, 39)])
+def test_prefix_random_mask(N, num_prev):
+    """The reference sweep's mask (run.py:181-203): row i keeps every key
+    j >= i and exactly min(num_prev, i) keys before it, chosen at random."""
+    cfg = dict(B=1, H=3, N=N, D=64, dtype=torch.float16, mask="prefix_random", num_prev=num_prev)
+    m = workloads.make_inputs(cfg, seed=2)[3][0]
+    i = torch.arange(N)
+    assert m[:, i[:, None] <= i[None, :]].all(), "every key j >= i is kept"
+    before = (m & (i[None, :] < i[:, None])).sum(-1)
+    assert torch.equal(before, torch.clamp(i, max=num_prev).expand_as(before))
+    if num_prev < N - 1:
+        assert not torch.equal(m[0], m[1]), "heads draw their own random keys"
+
+
+def test_sweep_shapes_follow_the_reference():
+    """run.py:497-540: B = 16 up to N = 1024, 4 up to 4096, 2 at 8192, 1 at
+    16384; then B 1..64 at N = 512; H12 D64 fp16, num_prev 2048."""
+    shapes = dict(workloads.sweep_shapes())
+    assert [c["B"] for n, c in shapes.items() if n.startswith("seq")] == [16, 16, 16, 16, 16, 4, 4, 2, 1]
+    assert [c["N"] for n, c in shapes.items() if n.startswith("seq")] == [64, 128, 256, 512, 1024, 2048, 4096,
+                                                                         8192, 16384]
+    assert [c["B"] for n, c in shapes.items() if n.startswith("batch")] == [1, 4, 8, 16, 32, 64]
+    assert all(c["H"] == 12 and c["D"] == 64 and c["num_prev"] == 2048 and c["dtype"] == torch.float16
+               for c in shapes.values())
+
+
 def test_roofline_arithmetic():
     assert workloads.dense_flops(16, 12, 512, 64) == 4 * 16 * 12 * 512 * 512 * 64
     b = workloads.attn_bytes(16, 12, 512, 64)
