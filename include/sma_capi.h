@@ -72,6 +72,11 @@ SMA_API int sma_pack_mask(const void* mask, void* packed, int64_t B, int64_t H, 
  * Supported: D in {64, 128}, 1 <= N <= SMA_MAX_SEQ_LEN, 16-byte aligned
  * q/k/v/out, scale finite and > 0 (the kernels fold the scale into the
  * exponent after the masked row max; the reference always passes 1/sqrt(D)).
+ * When the (batch*head, 128-row query tile) items are fewer than twice the
+ * SM count and at least 64 key tiles long, each item is split along keys
+ * over several SMs and merged; that path takes scratch (about
+ * items * pieces * 128 * (D + 4) floats) from a per-device stream-ordered
+ * pool the library keeps, released on `stream` after the launch.
  *
  * Replaces: forward()                          csrc/binding.cpp:9-47
  *           sparse_attention_fwd_fp16/_bf16()  csrc/sparse_attention.cu:149-185

@@ -41,6 +41,7 @@
 // The softmax reads its row's mask words of the next tile with one 16- or
 // 8-byte global load issued a tile ahead.
 // Every wait is bounded (mbar_wait_bounded) and reports through err_word.
+#include <algorithm>
 #include <cfloat>
 #include <cstdio>
 #include <cuda_bf16.h>
@@ -70,6 +71,7 @@ constexpr int kStages = 2;         // K ring and V ring depth per chain
 constexpr int kTmemCols = 512;
 constexpr int kChainCols = 256;
 constexpr int kScanBatch = 4;      // 16-byte mask loads in flight per thread while scanning
+constexpr int kSplitMinTiles = 32;  // key tiles per piece, at least, of an item split along keys
 constexpr int kPackBatch = 8;      // bool input: packed words (32 mask bytes each) per batch of loads in flight
 constexpr int kEpiGroups = 8;      // D = 128: mask rows of up to 8 16-byte groups (N <= 1024) scanned from registers
 
@@ -121,6 +123,7 @@ struct ChainCtl {
   uint32_t scan_bits[kSlots][kLiveWords];
   uint32_t live_bits[kSlots][kLiveWords];
   uint32_t n_live[kSlots];
+  uint32_t split_last;  // kSplitK: this chain's unit completed its item (broadcast to the warpgroup)
 };
 
 struct Ctl {
@@ -128,6 +131,31 @@ struct Ctl {
   uint32_t tmem_base;
   uint32_t abort_flag;
 };
+
+// Split along keys (kSplitK kernels), for workloads with fewer items than
+// chains: every item is cut into `pieces` units that share its live key tiles
+// evenly (by rank), run on different chains and leave their unnormalised O
+// (FP32) and (max, sums) in `ws`; the unit that completes its item's count in
+// `cnt` merges the item's pieces in piece order and writes O and the LSE.
+struct SplitParams {
+  int pieces;                // units per item (>= 2 in kSplitK kernels)
+  float* ws;                 // [units][128][4] (max, l, l_out, -) then [units][128][D]
+  unsigned long long* cnt;   // [items]: launch epoch << 8 | pieces finished
+  unsigned long long epoch;  // distinct per launch, < 2^56, never 0
+};
+
+// Counts one finished piece of an item; a counter left by an earlier launch
+// (another epoch, or whatever the memory held) counts as zero, so counters
+// need no clearing.  True for the piece that completes the item.
+__device__ __forceinline__ bool claim_last_piece(unsigned long long* cnt, unsigned long long epoch, int pieces) {
+  unsigned long long cur = *reinterpret_cast<volatile unsigned long long*>(cnt);
+  for (;;) {
+    const unsigned long long want = ((cur >> 8) == epoch) ? cur + 1ull : ((epoch << 8) | 1ull);
+    const unsigned long long prev = atomicCAS(cnt, cur, want);
+    if (prev == cur) return static_cast<int>(want & 0xFFull) == pieces;
+    cur = prev;
+  }
+}
 
 template <int D>
 constexpr size_t smem_bytes() {
@@ -266,6 +294,55 @@ __device__ __forceinline__ uint32_t group_live(const uint4& v, int g, int k, int
   }
 }
 
+// The unit that completed a split item merges the item's pieces p0 ..
+// p0+pieces-1 for its row r, in piece order: weights 2^(m_p - M) against the
+// row's overall max M, O = sum w_p O_p / sum w_p l_out_p, LSE from
+// sum w_p l_p (M = -inf: an empty row, O = 0 and LSE = -FLT_MAX).
+template <int D, bool BF16>
+__device__ __noinline__ void merge_pieces(const SplitParams sp, int64_t n_units, int64_t p0, int r, uint16_t* orow,
+                                          float* lse_r, bool write_o) {
+  const float* ml_base = sp.ws;                    // [unit][row][4]
+  const float* po_base = sp.ws + n_units * kBM * 4;  // [unit][row][D]
+  float M = -INFINITY;
+  for (int pc = 0; pc < sp.pieces; ++pc) M = fmaxf(M, __ldcg(ml_base + ((p0 + pc) * kBM + r) * 4));
+  float lr = 0.f, lo = 0.f;
+  for (int pc = 0; pc < sp.pieces; ++pc) {
+    const float4 v = __ldcg(reinterpret_cast<const float4*>(ml_base + ((p0 + pc) * kBM + r) * 4));
+    const float w = (v.x == -INFINITY) ? 0.f : ex2f(v.x - M);
+    lr += w * v.y;
+    lo += w * v.z;
+  }
+  const float inv = (lo > 0.f) ? (1.f / lo) : 0.f;
+#pragma unroll 1
+  for (int dc = 0; dc < D / 32; ++dc) {
+    float acc[32];
+#pragma unroll
+    for (int q = 0; q < 32; ++q) acc[q] = 0.f;
+    for (int pc = 0; pc < sp.pieces; ++pc) {
+      const float mp = __ldcg(ml_base + ((p0 + pc) * kBM + r) * 4);
+      const float w = (mp == -INFINITY) ? 0.f : ex2f(mp - M);
+      const float4* src = reinterpret_cast<const float4*>(po_base + ((p0 + pc) * kBM + r) * D + dc * 32);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const float4 o = __ldcg(src + q);
+        acc[4 * q] += w * o.x;
+        acc[4 * q + 1] += w * o.y;
+        acc[4 * q + 2] += w * o.z;
+        acc[4 * q + 3] += w * o.w;
+      }
+    }
+    uint32_t hw[16];
+#pragma unroll
+    for (int q = 0; q < 16; ++q) hw[q] = pack2<BF16>(acc[2 * q] * inv, acc[2 * q + 1] * inv);
+    if (write_o) {
+      uint4* dst = reinterpret_cast<uint4*>(orow + dc * 32);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) dst[q] = make_uint4(hw[4 * q], hw[4 * q + 1], hw[4 * q + 2], hw[4 * q + 3]);
+    }
+  }
+  if (lse_r != nullptr) *lse_r = (lr > 0.f) ? (M + log2f(lr)) * kLn2 : -FLT_MAX;
+}
+
 // Position of one chain in the flattened sequence of its live tiles.
 struct Cursor {
   int i;       // item index (-1 before the first item, n_items when exhausted)
@@ -290,7 +367,7 @@ __device__ __forceinline__ int next_live(const uint32_t* bits, int& w, uint32_t&
 // packed words; the softmax warps pack each item's rows into `pk` while they
 // scan them (pk then holds exactly what the mask packer writes) and the tile
 // loop reads its words back from there.  `mask` is unused then.
-template <int D, bool BF16, bool kBoolIn>
+template <int D, bool BF16, bool kBoolIn, bool kSplitK>
 __global__ void __launch_bounds__(kThreads, 1)
     attn_fwd_chain_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                           const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
@@ -298,7 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                           const uint8_t* __restrict__ bmask, uint32_t* pk,
                           const uint32_t* __restrict__ occ, float* __restrict__ lse, int N, int BH, int W,
                           int KT, int total_items, int vec, int o_wide, int head_major, int pf_early,
-                          float scale_log2, uint32_t* err_word,
+                          float scale_log2, const SplitParams sp, uint32_t* err_word,
                           uint64_t timeout_ns) {
   using C = ChainCfg<D>;
   constexpr int kBN = C::kBN;
@@ -333,6 +410,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int off = (full & 1) ? 2 * G - 1 - k : k;
     return full + (off < rem ? 1 : 0);
   };
+  // The item of chain c's unit i (kSplitK: units are pieces of items) and
+  // the piece it is (-1: a whole item).
+  auto item_at = [&](int c, int i) {
+    const int w = chain_item(c, i);
+    return item_of(kSplitK ? w / sp.pieces : w, BH, QT, N, head_major);
+  };
+  auto piece_at = [&](int c, int i) { return kSplitK ? chain_item(c, i) % sp.pieces : -1; };
 
   if (threadIdx.x == 256) {
     for (int c = 0; c < 2; ++c) {
@@ -467,7 +551,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t gk = 0, gv = 0, q_count = 0;  // K, V and Q copies issued
       bool ok = true;
       auto issue_k = [&]() -> bool {
-        const Item it = item_of(chain_item(c, kc.i), BH, QT, N, head_major);
+        const Item it = item_at(c, kc.i);
         if (kc.t == 0) {
           // First tile of an item: its Q, into the buffer the item kQBufs back used.
           const int qb = q_count % C::kQBufs;
@@ -496,7 +580,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         return true;
       };
       auto issue_v = [&]() -> bool {
-        const Item it = item_of(chain_item(c, vc.i), BH, QT, N, head_major);
+        const Item it = item_at(c, vc.i);
         const int stage = gv % kStages;
         if (gv >= static_cast<uint32_t>(kStages) &&
             !mbar_wait_bounded(smem_u32(&cc.v_empty[stage]), ((gv / kStages) - 1) & 1, abort_flag, timeout_ns))
@@ -823,7 +907,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // one (two words per item: the map is only made for N <= 8192).
       const uint32_t* occ_j = nullptr;
       if (occ != nullptr) {
-        const Item itj = item_of(chain_item(c, j), BH, QT, N, head_major);
+        const Item itj = item_at(c, j);
         occ_j = occ + 2 * (static_cast<int64_t>(itj.bh) * QT + itj.q0 / kBM);
       }
       const int nw = (KT + 31) >> 5;  // <= 32: one word per lane
@@ -836,8 +920,33 @@ __global__ void __launch_bounds__(kThreads, 1)
           cc.scan_bits[slot][lane] = 0u;  // ready for the item four later
         }
         if (KT - lane * 32 < 32) x &= (1u << (KT - lane * 32)) - 1u;
-        cc.live_bits[slot][lane] = x;
       }
+      if constexpr (kSplitK) {
+        // This unit's share of the item's L live tiles: those of rank
+        // [pj * L / pieces, (pj + 1) * L / pieces) in key order.
+        const int pj = piece_at(c, j);
+        const uint32_t cnt = static_cast<uint32_t>(__popc(x));
+        uint32_t incl = cnt;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+          const uint32_t t = __shfl_up_sync(0xffffffffu, incl, off);
+          if (lane >= off) incl += t;
+        }
+        const int live = static_cast<int>(__shfl_sync(0xffffffffu, incl, 31));
+        const int pre = static_cast<int>(incl - cnt);
+        const int a = max(pj * live / sp.pieces - pre, 0);
+        const int b = min((pj + 1) * live / sp.pieces - pre, static_cast<int>(cnt));
+        uint32_t keep = 0u;
+        if (b > a) {
+          keep = x;
+          for (int t = 0; t < a; ++t) keep &= keep - 1u;  // drop the a lowest
+          uint32_t above = keep;
+          for (int t = 0; t < b - a; ++t) above &= above - 1u;
+          keep &= ~above;  // the next b - a
+        }
+        x = keep;
+      }
+      if (lane < nw) cc.live_bits[slot][lane] = x;
       const uint32_t n = __reduce_add_sync(0xffffffffu, static_cast<uint32_t>(__popc(x)));
       __syncwarp();
       if (lane == 0) {
@@ -851,12 +960,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     // HBM at once, and the first list is published before the second is built.
     const int n_pre = n_items < 2 ? n_items : 2;
     if constexpr (kBoolIn) {
-      for (int j = 0; j < n_pre; ++j) prefetch_bool_row(item_of(chain_item(c, j), BH, QT, N, head_major));
+      for (int j = 0; j < n_pre; ++j) prefetch_bool_row(item_at(c, j));
     } else {
-      if (n_pre > 1 && occ == nullptr) prefetch_rows_l1(item_of(chain_item(c, 1), BH, QT, N, head_major));
+      if (n_pre > 1 && occ == nullptr) prefetch_rows_l1(item_at(c, 1));
     }
     for (int j = 0; j < n_pre; ++j) {
-      if (occ == nullptr) scan_item(item_of(chain_item(c, j), BH, QT, N, head_major), j);
+      if (occ == nullptr) scan_item(item_at(c, j), j);
       named_bar_sync(bar_id, 128);
       if (wq == 0) publish(j);
     }
@@ -865,7 +974,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     bool have_mw = false;  // mw already holds tile 0 of the current item
     for (int i = 0; i < n_items; ++i) {
       const int slot = i % kSlots;
-      const Item it = item_of(chain_item(c, i), BH, QT, N, head_major);
+      const Item it = item_at(c, i);
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_u32(&cc.sched_full[slot]), (i / kSlots) & 1,
                                                               abort_flag, timeout_ns));
       const uint32_t n = ok ? cc.n_live[slot] : 0u;
@@ -873,7 +982,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // (at the item's last tile instead when the rows of a round of items
       // would not fit in L2 together).
       if constexpr (kBoolIn) {
-        if (pf_early && i + 2 < n_items) prefetch_bool_row(item_of(chain_item(c, i + 2), BH, QT, N, head_major));
+        if (pf_early && i + 2 < n_items) prefetch_bool_row(item_at(c, i + 2));
       }
       // Walk over the item's live bits (word lw, bits above the current tile lx).
       int lw = 0;
@@ -889,7 +998,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         int next_kt = -1;
         if constexpr (kBoolIn) {
           if (!pf_early && t + 1 == n && i + 2 < n_items)
-            prefetch_bool_row(item_of(chain_item(c, i + 2), BH, QT, N, head_major));
+            prefetch_bool_row(item_at(c, i + 2));
         }
         if (t + 1 == n && i + 1 < n_items) {
           const int slot2 = (i + 1) % kSlots;
@@ -928,7 +1037,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (t + 1 < n) {
           fetch_words(it, next_live(cc.live_bits[slot], lw, lx), mw);
         } else if (next_kt >= 0) {
-          fetch_words(item_of(chain_item(c, i + 1), BH, QT, N, head_major), next_kt, mw);
+          fetch_words(item_at(c, i + 1), next_kt, mw);
           have_mw = true;
         }
 
@@ -1003,7 +1112,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       // wait for the last PV, so the loads after it hit (a prefetch holds no
       // registers).
       const bool do_scan = i + 2 < n_items;
-      const Item itn = item_of(chain_item(c, do_scan ? i + 2 : i), BH, QT, N, head_major);
+      const Item itn = item_at(c, do_scan ? i + 2 : i);
       // D = 128 loads short rows (up to kEpiGroups 16-byte groups) outright
       // below, before it writes O.
       const bool scan_regs = !kBoolIn && !C::kStageO && vec && G4 <= kEpiGroups;
@@ -1016,7 +1125,48 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (n > 0 && !ready) ok = false;
         return ready;
       };
-      if constexpr (C::kStageO) {
+      if constexpr (kSplitK) {
+        // A piece of a split item (no O staging, no scan ahead: i+2 is
+        // scanned below like any unit).  Its unnormalised O (FP32) and (max,
+        // sums) go to the workspace; the piece that completes the item's
+        // count merges the item's pieces in piece order, so the result does
+        // not depend on which piece finishes last.
+        if (do_scan && occ == nullptr) scan_item(itn, i + 2);
+        named_bar_sync(bar_id, 128);
+        if (wq == 0 && do_scan) publish(i + 2);
+        const int w = chain_item(c, i);
+        const int item = w / sp.pieces;
+        const int64_t n_units = static_cast<int64_t>(total_items);
+        float* ml = sp.ws + (static_cast<int64_t>(w) * kBM + r) * 4;
+        float* po = sp.ws + n_units * kBM * 4 + (static_cast<int64_t>(w) * kBM + r) * D;
+        const bool o_ready = wait_o();
+#pragma unroll 1
+        for (int dc = 0; dc < D / 32; ++dc) {
+          uint32_t u[32];
+          if (o_ready) {
+            tmem_ld32(t_lane + kOCol + dc * 32, u);
+            tmem_wait_ld();
+          } else {
+#pragma unroll
+            for (int q = 0; q < 32; ++q) u[q] = 0u;
+          }
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            reinterpret_cast<uint4*>(po + dc * 32)[q] = make_uint4(u[4 * q], u[4 * q + 1], u[4 * q + 2], u[4 * q + 3]);
+        }
+        *reinterpret_cast<float4*>(ml) = make_float4(m_run, l_run, l_out, 0.f);
+        __threadfence();
+        named_bar_sync(bar_id, 128);
+        if (r == 0) cc.split_last = claim_last_piece(sp.cnt + item, sp.epoch, sp.pieces) ? 1u : 0u;
+        named_bar_sync(bar_id, 128);
+        if (cc.split_last != 0u && r < it.rows_valid) {
+          __threadfence();
+          merge_pieces<D, BF16>(sp, n_units, static_cast<int64_t>(item) * sp.pieces, r,
+                                out + (static_cast<int64_t>(it.bh) * N + it.q0 + r) * D,
+                                lse != nullptr ? lse + static_cast<int64_t>(it.bh) * N + it.q0 + r : nullptr,
+                                ctl.abort_flag == 0);
+        }
+      } else if constexpr (C::kStageO) {
         // The work that does not need O goes first, under the last PV's
         // latency: the scan of item i+2, the barrier that also frees the
         // staging tile (the previous item's O store has read it), and the
@@ -1127,8 +1277,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ---------------------------------------------------------------- host side
 
-template <int D, bool BF16, bool kBoolIn>
-int launch(const AttnParams& p, const char** msg) {
+template <int D, bool BF16, bool kBoolIn, bool kSplitK>
+int launch(const AttnParams& p, int pieces, const char** msg) {
   using C = ChainCfg<D>;
   constexpr size_t kSmemBytes = smem_bytes<D>();
   const int64_t BH = p.B * p.H;
@@ -1136,7 +1286,8 @@ int launch(const AttnParams& p, const char** msg) {
   const int64_t W = (N + 31) / 32;
   const int64_t KT = (N + C::kBN - 1) / C::kBN;
   const int64_t QT = (N + kBM - 1) / kBM;
-  const int64_t total = QT * BH;
+  const int64_t items = QT * BH;
+  const int64_t total = kSplitK ? items * pieces : items;  // work units
   if (total > 0x3FFFFFFFll) {
     *msg = "attention: batch*heads too large";
     return kErrArg;
@@ -1153,7 +1304,7 @@ int launch(const AttnParams& p, const char** msg) {
   DeviceProps dp;
   if (!device_props(&dp, msg)) return kErrCuda;
   static std::atomic<bool> smem_set[kMaxDevices] = {};
-  auto kern = attn_fwd_chain_kernel<D, BF16, kBoolIn>;
+  auto kern = attn_fwd_chain_kernel<D, BF16, kBoolIn, kSplitK>;
   {
     cudaError_t e = ensure_smem_limit(kern, kSmemBytes, dp.device, smem_set);
     if (e != cudaSuccess) {
@@ -1174,12 +1325,32 @@ int launch(const AttnParams& p, const char** msg) {
   // starts if two rounds of items' rows (2 chains per CTA) take at most 48
   // MB of L2, else at item i's last tile.
   const int pf_early = 2 * static_cast<int64_t>(grid) * 2 * kBM * N <= (int64_t{48} << 20) ? 1 : 0;
+  SplitParams sp{};
+  void* ws = nullptr;
+  if constexpr (kSplitK) {
+    // Counters (one per item), then (max, sums) and the FP32 O of every unit.
+    const size_t cnt_bytes = (static_cast<size_t>(items) * 8 + 255) / 256 * 256;
+    const size_t rows = static_cast<size_t>(total) * kBM;
+    cudaError_t ea = scratch_alloc_async(&ws, cnt_bytes + rows * (4 + D) * sizeof(float), p.stream);
+    if (ea != cudaSuccess) {
+      *msg = cudaGetErrorString(ea);
+      return kErrCuda;
+    }
+    sp.pieces = pieces;
+    sp.cnt = static_cast<unsigned long long*>(ws);
+    sp.ws = reinterpret_cast<float*>(static_cast<uint8_t*>(ws) + cnt_bytes);
+    sp.epoch = next_launch_epoch();
+  }
   cudaError_t e = launch_pdl(kern, static_cast<unsigned>(grid), kThreads, kSmemBytes, p.stream, mq, mk, mv, mo,
                              static_cast<uint16_t*>(p.out), kBoolIn ? nullptr : p.mask, kBoolIn ? p.bmask : nullptr,
                              kBoolIn ? p.packed_out : nullptr, occ, p.lse, static_cast<int>(N), static_cast<int>(BH),
                              static_cast<int>(W), static_cast<int>(KT), static_cast<int>(total), vec, o_wide,
-                             head_major, pf_early, p.scale * kLog2e, p.err_word, p.timeout_ns);
+                             head_major, pf_early, p.scale * kLog2e, sp, p.err_word, p.timeout_ns);
   if (e == cudaSuccess) e = cudaGetLastError();
+  if (ws != nullptr) {
+    cudaError_t ef = cudaFreeAsync(ws, p.stream);
+    if (e == cudaSuccess) e = ef;
+  }
   if (e != cudaSuccess) {
     static thread_local char buf[256];
     cudaFuncAttributes fa{};
@@ -1198,13 +1369,32 @@ bool chain_supported(const AttnParams& p) {
   return (p.D == 64 && p.N <= ChainCfg<64>::kMaxN) || (p.D == 128 && p.N <= ChainCfg<128>::kMaxN);
 }
 
-int launch_attn_fwd_chain(const AttnParams& p, const char** msg) {
-  if (p.bmask != nullptr) {
-    if (p.D == 128) return p.dtype == 1 ? launch<128, true, true>(p, msg) : launch<128, false, true>(p, msg);
-    return p.dtype == 1 ? launch<64, true, true>(p, msg) : launch<64, false, true>(p, msg);
+template <bool kBoolIn>
+int launch_any(const AttnParams& p, int pieces, const char** msg) {
+  if (pieces >= 2) {
+    if (p.D == 128)
+      return p.dtype == 1 ? launch<128, true, kBoolIn, true>(p, pieces, msg) : launch<128, false, kBoolIn, true>(p, pieces, msg);
+    return p.dtype == 1 ? launch<64, true, kBoolIn, true>(p, pieces, msg) : launch<64, false, kBoolIn, true>(p, pieces, msg);
   }
-  if (p.D == 128) return p.dtype == 1 ? launch<128, true, false>(p, msg) : launch<128, false, false>(p, msg);
-  return p.dtype == 1 ? launch<64, true, false>(p, msg) : launch<64, false, false>(p, msg);
+  if (p.D == 128)
+    return p.dtype == 1 ? launch<128, true, kBoolIn, false>(p, 1, msg) : launch<128, false, kBoolIn, false>(p, 1, msg);
+  return p.dtype == 1 ? launch<64, true, kBoolIn, false>(p, 1, msg) : launch<64, false, kBoolIn, false>(p, 1, msg);
+}
+
+int launch_attn_fwd_chain(const AttnParams& p, const char** msg) {
+  // Split along keys when the items (batch*head x 128-row query tiles) leave
+  // chains idle and are long: as many pieces per item as fill the chains,
+  // each of at least kSplitMinTiles key tiles (shorter pieces lose to the
+  // merge and the per-unit fixed costs).
+  DeviceProps dp;
+  if (!device_props(&dp, msg)) return kErrCuda;
+  const int64_t items = (p.N + kBM - 1) / kBM * p.B * p.H;
+  const int64_t kt = p.D == 64 ? (p.N + 127) / 128 : (p.N + 63) / 64;
+  const int64_t chains = 2 * static_cast<int64_t>(dp.sms);
+  int pieces = 1;
+  if (items > 0 && items < chains)
+    pieces = static_cast<int>(std::min<int64_t>({kt / kSplitMinTiles, chains / items, 255}));
+  return p.bmask != nullptr ? launch_any<true>(p, pieces, msg) : launch_any<false>(p, pieces, msg);
 }
 
 }  // namespace sma

@@ -94,6 +94,13 @@ CUresult make_tensor_map_3d_f32(CUtensorMap* m, const void* ptr, int64_t D, int6
 // Message for a failed tensor-map encode: `what` and the driver status.
 const char* tensor_map_error(const char* what, CUresult rc);
 
+// Stream-ordered scratch from a per-device memory pool that keeps its memory
+// between calls (no release back to the driver), so a steady stream of
+// launches allocates only once.  Freed with cudaFreeAsync on the same stream.
+cudaError_t scratch_alloc_async(void** p, size_t bytes, cudaStream_t stream);
+// A value distinct for every call in the process: 56 bits, never 0.
+unsigned long long next_launch_epoch();
+
 // Devices the per-device caches of the launchers cover.
 constexpr int kMaxDevices = 64;
 

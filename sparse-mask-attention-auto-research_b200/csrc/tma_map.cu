@@ -3,6 +3,7 @@
 // (cudaGetDriverEntryPoint), so the library does not link libcuda.
 #include <cudaTypedefs.h>
 
+#include <atomic>
 #include <cstdio>
 #include <mutex>
 
@@ -81,6 +82,41 @@ CUresult make_tensor_map_3d_f32(CUtensorMap* m, const void* ptr, int64_t D, int6
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(ptr), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+namespace {
+struct PoolSlot {
+  std::once_flag once;
+  cudaMemPool_t pool = nullptr;
+  cudaError_t err = cudaSuccess;
+};
+PoolSlot g_pools[kMaxDevices];
+std::atomic<unsigned long long> g_epoch{0};
+}  // namespace
+
+cudaError_t scratch_alloc_async(void** p, size_t bytes, cudaStream_t stream) {
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+  PoolSlot& s = g_pools[dev];
+  std::call_once(s.once, [&]() {
+    cudaMemPoolProps props{};
+    props.allocType = cudaMemAllocationTypePinned;
+    props.location.type = cudaMemLocationTypeDevice;
+    props.location.id = dev;
+    s.err = cudaMemPoolCreate(&s.pool, &props);
+    if (s.err == cudaSuccess) {
+      uint64_t keep = ~uint64_t{0};
+      s.err = cudaMemPoolSetAttribute(s.pool, cudaMemPoolAttrReleaseThreshold, &keep);
+    }
+  });
+  if (s.err != cudaSuccess) return s.err;
+  return cudaMallocFromPoolAsync(p, bytes, s.pool, stream);
+}
+
+unsigned long long next_launch_epoch() {
+  return ((g_epoch.fetch_add(1, std::memory_order_relaxed) + 1) & ((1ull << 55) - 1)) | (1ull << 55);
 }
 
 const char* tensor_map_error(const char* what, CUresult rc) {

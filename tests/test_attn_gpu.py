@@ -267,3 +267,50 @@ def test_partial_last_round(H, N, D, dtype):
     ref_lse = oracle.lse(q.float().cpu().numpy(), k.float().cpu().numpy(), m.cpu().numpy(), 1 / math.sqrt(D))
     check_against(o1, l1, torch.from_numpy(ref_out), torch.from_numpy(ref_lse), m, dtype,
                   name=f"partial last round H{H} N{N} D{D} {str(dtype)[6:]}")
+
+
+def _split_pieces(B, H, N, D):
+    """Pieces per item the forward cuts along keys (its host-side rule):
+    fewer items than chains (two per SM), at least 32 key tiles a piece."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    items = B * H * ((N + 127) // 128)
+    kt = (N + 127) // 128 if D == 64 else (N + 63) // 64
+    if items >= 2 * sms:
+        return 1
+    return min(kt // 32, 2 * sms // items, 255)
+
+
+@pytest.mark.parametrize("B,H,N,D,dtype", [(1, 1, 8192, 64, torch.float16), (1, 1, 4096, 128, torch.bfloat16),
+                                           (1, 1, 6000, 128, torch.float16), (1, 2, 8320, 64, torch.bfloat16),
+                                           (1, 1, 12288, 128, torch.bfloat16)])
+def test_split_along_keys(B, H, N, D, dtype):
+    """Few items, long rows: each item is cut into pieces of at least 32 key
+    tiles that share its live tiles, and the last piece to finish merges
+    them.  Against the oracle on sampled rows (first and last query tiles,
+    fully masked rows, a row whose only key is the last one, dead key tiles,
+    a fully masked head, ragged N), and bit-identical across runs: the merge
+    runs in piece order whichever piece finishes last."""
+    g = torch.Generator(device=DEV).manual_seed(B * H * N + D)
+    q, k, v = (torch.randn(B, H, N, D, generator=g, device=DEV).to(dtype) for _ in range(3))
+    m = torch.rand(B, H, N, N, generator=g, device=DEV) < 0.05
+    m[..., :300, 128:2600] = False       # dead key tiles for the first query tiles
+    m[..., 5, :] = False                 # a fully masked row
+    m[..., 9, :] = False
+    m[..., 9, N - 1] = True              # a row whose only key is the last one
+    if H > 1:
+        m[:, 1] = False                  # a fully masked head
+    if torch.cuda.get_device_properties(0).multi_processor_count == 148:
+        assert _split_pieces(B, H, N, D) >= 2
+    o1, l1 = run_fwd(q, k, v, m)
+    o2, l2 = run_fwd(q, k, v, m)
+    assert torch.equal(o1, o2) and torch.equal(l1, l2)
+    rows = torch.cat([torch.arange(0, 160), torch.randperm(N, generator=torch.Generator().manual_seed(2))[:200],
+                      torch.arange(N - 140, N)]).unique().to(DEV)
+    qs, ms = q[:, :, rows].float().cpu().numpy(), m[:, :, rows].cpu().numpy()
+    kf, vf = k.float().cpu().numpy(), v.float().cpu().numpy()
+    ref_out = oracle.attention(qs, kf, vf, ms, 1 / math.sqrt(D))
+    ref_lse = oracle.lse(qs, kf, ms, 1 / math.sqrt(D))
+    check_against(o1[:, :, rows], l1[:, :, rows], torch.from_numpy(ref_out), torch.from_numpy(ref_lse),
+                  torch.from_numpy(ms), dtype, name=f"split B{B} H{H} N{N} D{D} {str(dtype)[6:]}")
+    # The public API (pack + forward) returns the same bits.
+    assert torch.equal(sparse_attention(q, k, v, m), o1)
