@@ -208,3 +208,19 @@ def test_items_without_live_tiles_between_live_items(empty_rounds):
     mf = m.reshape(BH, N, N)[heads].unsqueeze(0).cpu()
     want = oracle.attention_backward(qf, kf, vf, mf.numpy(), 1 / math.sqrt(D), df)
     check_grads(sub, want, q.dtype, mf)
+
+
+def test_backward_after_forward_split_along_keys():
+    """Few long items: the forward splits each along keys and merges (O and
+    LSE from the merge); the backward consumes them.  Gradients against the
+    oracle."""
+    B, H, N, D, dtype = 1, 1, 4096, 128, torch.bfloat16
+    g = torch.Generator(device=DEV).manual_seed(31)
+    q, k, v = (torch.randn(B, H, N, D, generator=g, device=DEV).to(dtype) for _ in range(3))
+    m = torch.rand(B, H, N, N, generator=g, device=DEV) < 0.05
+    m[..., 3, :] = False  # a fully masked row
+    dout = torch.randn(q.shape, generator=g, device=DEV).to(dtype)
+    got = fwd_bwd(q, k, v, m, dout)
+    want = oracle.attention_backward(*(x.float().cpu().numpy() for x in (q, k, v)), m.cpu().numpy(),
+                                     1 / math.sqrt(D), dout.float().cpu().numpy())
+    check_grads(got, want, dtype, m.cpu())
