@@ -1021,16 +1021,26 @@ __global__ void __launch_bounds__(kThreads, 1)
         arrive_warp(cc.s_free);  // the next QK^T may overwrite S now
 
         float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+        // A tile every row of the warp keeps whole (dense or prefix-shaped
+        // masks) needs the max only.
+        uint32_t all_words = mw[0];
 #pragma unroll
-        for (int ch = 0; ch < kWords; ++ch) {
-          const uint32_t word = mw[ch];
+        for (int ch = 1; ch < kWords; ++ch) all_words &= mw[ch];
+        if (__all_sync(0xffffffffu, all_words == 0xFFFFFFFFu)) {
 #pragma unroll
-          for (int jj = 0; jj < 32; jj += 2) {
-            const float v0 = (word & (1u << jj)) ? s[ch * 32 + jj] : -INFINITY;
-            const float v1 = (word & (2u << jj)) ? s[ch * 32 + jj + 1] : -INFINITY;
-            s[ch * 32 + jj] = v0;
-            s[ch * 32 + jj + 1] = v1;
-            mx[(jj >> 1) & 3] = max3f(mx[(jj >> 1) & 3], v0, v1);
+          for (int e = 0; e < kBN; e += 2) mx[(e >> 1) & 3] = max3f(mx[(e >> 1) & 3], s[e], s[e + 1]);
+        } else {
+#pragma unroll
+          for (int ch = 0; ch < kWords; ++ch) {
+            const uint32_t word = mw[ch];
+#pragma unroll
+            for (int jj = 0; jj < 32; jj += 2) {
+              const float v0 = (word & (1u << jj)) ? s[ch * 32 + jj] : -INFINITY;
+              const float v1 = (word & (2u << jj)) ? s[ch * 32 + jj + 1] : -INFINITY;
+              s[ch * 32 + jj] = v0;
+              s[ch * 32 + jj + 1] = v1;
+              mx[(jj >> 1) & 3] = max3f(mx[(jj >> 1) & 3], v0, v1);
+            }
           }
         }
         // The next tile's mask words, a whole tile of exponentials ahead of their use.
