@@ -226,6 +226,21 @@ def p50(xs):
     return statistics.median(xs)
 
 
+def back_to_back_ms(fn, stream, warmup=10, repeat=50):
+    """The reference's own timing (run.py:206-217): `repeat` back-to-back
+    calls between two events after `warmup`, no flush, the mean per call."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(repeat):
+        fn()
+    b.record(stream)
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / repeat
+
+
 def max_over_ranks(vals, dev, world):
     t = torch.tensor(vals, dtype=torch.float64, device=dev)
     if world > 1:
@@ -454,8 +469,10 @@ def run_reference_cuda(args):
         st = [s[0] for s in time_steps(step, n, flush, stream, marks=1)]
         sp = time_steps(step, n, flush, stream, marks=2)
         attn_mean = statistics.fmean([s[1] for s in sp])
+        ev2 = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+        b2b = back_to_back_ms(lambda: step(ev2), stream)
         rl = attn_roofline(name, B, H, N, D, m, attn_mean, peaks)
-        results[name] = {"step_ms_p50": p50(st), "pack_ms_p50": p50([s[0] for s in sp]),
+        results[name] = {"step_ms_p50": p50(st), "back_to_back_ms_mean": b2b, "pack_ms_p50": p50([s[0] for s in sp]),
                          "attn_ms_p50": p50([s[1] for s in sp]), "attn_ms_mean": attn_mean,
                          "tflops_dense_equiv": workloads.dense_flops(B, H, N, D) / (p50(st) * 1e-3) / 1e12,
                          "roofline_frac": rl["frac"], "bound": rl["bound"], "steps": n}
@@ -531,6 +548,8 @@ def run_ours(args):
 
     # The two kernels timed apart, in a second pass of the same steps.
     split = time_steps(step, min(args.steps, 500), flush, stream, marks=2)
+    # The reference's own timing of the same call: 50 back to back, no flush, mean.
+    b2b_ms = max_over_ranks([back_to_back_ms(step, stream)], dev, world)[0]
     pack_ms = [s[0] for s in split]
     attn_ms = [s[1] for s in split]
     p50_step, mean_step, p50_attn, mean_attn, p50_pack, mean_pack = max_over_ranks(
@@ -652,6 +671,7 @@ def run_ours(args):
         "clocks": clocks,
         "gpu_launches": 2 * args.steps,
         "split_pass_steps": len(split),
+        "back_to_back_ms_mean": b2b_ms,
         "timed_wall_s": wall,
     }
     if gather_ms is not None:
