@@ -1167,7 +1167,13 @@ __global__ void __launch_bounds__(kThreads, 1)
         *reinterpret_cast<float4*>(ml) = make_float4(m_run, l_run, l_out, 0.f);
         __threadfence();
         named_bar_sync(bar_id, 128);
-        if (r == 0) cc.split_last = claim_last_piece(sp.cnt + item, sp.epoch, sp.pieces) ? 1u : 0u;
+        if (r == 0) {
+          const bool last = claim_last_piece(sp.cnt + item, sp.epoch, sp.pieces);
+          // The item's count starts from zero again, so a replay of the same
+          // launch (a CUDA graph: same workspace, same epoch) counts afresh.
+          if (last) atomicExch(sp.cnt + item, 0ull);
+          cc.split_last = last ? 1u : 0u;
+        }
         named_bar_sync(bar_id, 128);
         if (cc.split_last != 0u && r < it.rows_valid) {
           __threadfence();
