@@ -1073,7 +1073,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
         const uint64_t scale2 = f2(scale_log2, scale_log2);
         const uint64_t negm2 = f2(-m_use, -m_use);
-        float la[2] = {0.f, 0.f};
+        // Row sums, two keys per add (f32x2): la2 of P as computed, lr2
+        // (bf16) of P as rounded for the PV product.
+        uint64_t la2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
         uint64_t lr2[2] = {f2(0.f, 0.f), f2(0.f, 0.f)};
 #pragma unroll
         for (int ch = 0; ch < kWords; ++ch) {
@@ -1085,14 +1087,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             const float p0 = ex2f(x0);
             const float p1 = ex2f(x1);
             pk[jj] = pack2<BF16>(p0, p1);
-            la[jj & 1] += p0 + p1;
+            la2[jj & 1] = add2(la2[jj & 1], f2(p0, p1));
             if constexpr (BF16) {
               lr2[jj & 1] = add2(lr2[jj & 1], f2(__uint_as_float(pk[jj] << 16), __uint_as_float(pk[jj] & 0xFFFF0000u)));
             }
           }
           tmem_st16(t_lane + kPCol + ch * 16, pk);
         }
-        float lr[2];
+        float la[2], lr[2];
+        f2_split(add2(la2[0], la2[1]), la[0], la[1]);
         f2_split(add2(lr2[0], lr2[1]), lr[0], lr[1]);
         if (__any_sync(0xffffffffu, rescale)) {
           // Rare: the running max rose by more than the threshold; bring O
