@@ -144,10 +144,35 @@ struct BwdCtl {
 };
 
 // Shared memory: K[kKVBufs] | V[kKVBufs] | Q[kQBufs] | dO[kQBufs] | dS[kDSBufs]
-// | mask words [kQBufs][4][128] | lse2 [kQBufs][128] | Delta [kQBufs][128] |
+// | mask words [kQBufs][4][128] | -lse2 [kQBufs][128] | -Delta [kQBufs][128] |
 // dQ staging [4 warps][kStageBoxes][32][32] FP32 | control (with the live lists).
 static_assert(BwdCfg<64>::kOffCtl + sizeof(BwdCtl) <= BwdCfg<64>::kSmemBytes, "shared memory layout");
 static_assert(BwdCfg<128>::kOffCtl + sizeof(BwdCtl) <= BwdCfg<128>::kSmemBytes, "shared memory layout");
+
+// Packed FP32 pairs (sm_100a f32x2 instructions): one issue slot for two lanes' worth of FMA / add / multiply.
+__device__ __forceinline__ uint64_t f2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t fma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t add2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ uint64_t mul2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
 
 __device__ __forceinline__ float ex2f(float x) {
   float y;
@@ -252,7 +277,8 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
   }
   BwdCtl& ctl = *reinterpret_cast<BwdCtl*>(smem + C::kOffCtl);
   // Per buffer b: word w of query row i at s_mask[b * 4 * kT + w * kT + i];
-  // LSE * log2(e) and Delta per query row at s_lse / s_delta [b * kT + i].
+  // -LSE * log2(e) and -Delta per query row at s_lse / s_delta [b * kT + i]
+  // (negated, so that the element-wise pass adds them in packed pairs).
   uint32_t* s_mask = reinterpret_cast<uint32_t*>(smem + C::kOffMask);
   float* s_lse = reinterpret_cast<float*>(smem + C::kOffLse);
   float* s_delta = reinterpret_cast<float*>(smem + C::kOffDelta);
@@ -385,10 +411,10 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
         const int i = lane + 32 * rr;
 #pragma unroll
         for (int w = 0; w < 4; ++w) s_mask[b * 4 * kT + w * kT + i] = w4[rr][w] & valid_bits(kt * 4 + w, N);
-        // -FLT_MAX (a row with no kept key) becomes -inf; such a row has no
-        // mask bit, so its P is 0 by the select and never uses this value.
-        s_lse[b * kT + i] = l2[rr] * kLog2e;
-        s_delta[b * kT + i] = de[rr];
+        // -FLT_MAX (a row with no kept key) becomes +inf here; such a row has
+        // no mask bit, so its P is 0 by the select and never uses this value.
+        s_lse[b * kT + i] = -(l2[rr] * kLog2e);
+        s_delta[b * kT + i] = -de[rr];
       }
       __syncwarp();
       if (lane == 0) {
@@ -722,7 +748,8 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
       // ============================================================== compute
       const float c2 = scale * kLog2e;
       const int my_word = (t >> 5) * kT;  // the word holding this key, for each query row
-      const int kb = t & 31;
+      const uint32_t kbit = 1u << (t & 31);  // this key's bit in a query row's mask word
+      const uint64_t c2x2 = f2(c2, c2);
       for (int j = 0; ok && j < n_items; ++j) {
         ok = wait_all(ctl.item_full[j % kSlots], (j / kSlots) & 1);
         if (!ok) break;
@@ -748,13 +775,14 @@ __global__ void __launch_bounds__(BwdCfg<D>::kThreads, 1)
               const float4 l4 = *reinterpret_cast<const float4*>(t_lse + c * 32 + e);
               const float4 d4 = *reinterpret_cast<const float4*>(t_delta + c * 32 + e);
               const uint32_t mm[4] = {m4.x, m4.y, m4.z, m4.w};
-              const float ll[4] = {l4.x, l4.y, l4.z, l4.w}, dd[4] = {d4.x, d4.y, d4.z, d4.w};
-              float p[4], ds[4];
+              // x = s * scale * log2(e) - lse2 and ds = p * (dp - Delta), two queries per instruction.
+              float x[4], p[4], ds[4];
+              f2_split(fma2(f2(s[e], s[e + 1]), c2x2, f2(l4.x, l4.y)), x[0], x[1]);
+              f2_split(fma2(f2(s[e + 2], s[e + 3]), c2x2, f2(l4.z, l4.w)), x[2], x[3]);
 #pragma unroll
-              for (int u = 0; u < 4; ++u) {
-                p[u] = ((mm[u] >> kb) & 1u) ? ex2f(fmaf(s[e + u], c2, -ll[u])) : 0.f;
-                ds[u] = p[u] * (dp[e + u] - dd[u]);
-              }
+              for (int u = 0; u < 4; ++u) p[u] = (mm[u] & kbit) ? ex2f(x[u]) : 0.f;
+              f2_split(mul2(f2(p[0], p[1]), add2(f2(dp[e], dp[e + 1]), f2(d4.x, d4.y))), ds[0], ds[1]);
+              f2_split(mul2(f2(p[2], p[3]), add2(f2(dp[e + 2], dp[e + 3]), f2(d4.z, d4.w))), ds[2], ds[3]);
               pw[e / 2] = pack2<BF16>(p[0], p[1]);
               pw[e / 2 + 1] = pack2<BF16>(p[2], p[3]);
               dw[e / 2] = pack2<BF16>(ds[0], ds[1]);
