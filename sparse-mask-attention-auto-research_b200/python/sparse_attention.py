@@ -21,6 +21,9 @@ Differences from the reference, all deliberate:
   * ``SparseAttentionFunction.backward`` runs the backward kernel; the
     reference's CUDA backward is an unbound stub (AttributeError when
     called) and its CPU formulas define the result.
+  * ``sparse_attention`` builds the autograd node only when an input
+    requires a gradient; otherwise it runs the same forward (O and the LSE)
+    directly, which saves the node's host cost (same results).
   * ``sparse_attention`` / ``sparse_attention_func`` pack long or large
     masks with the fused packer, which also writes the per-query-tile map of
     live key tiles the attention kernel then uses (same results, no
@@ -94,7 +97,14 @@ def sparse_attention(q, k, v, mask):
     if orig_dtype == torch.float32:
         q, k, v = q.bfloat16(), k.bfloat16(), v.bfloat16()
     mask_packed, occupancy = _pack_for_attention(mask, D)
-    out = SparseAttentionFunction.apply(q, k, v, mask_packed, mask, scale, N, occupancy)
+    if torch.is_grad_enabled() and (q.requires_grad or k.requires_grad or v.requires_grad):
+        out = SparseAttentionFunction.apply(q, k, v, mask_packed, mask, scale, N, occupancy)
+    else:
+        # Nothing to differentiate: the same forward (O and the LSE) without
+        # the autograd node.
+        out = torch.empty_like(q)
+        lse = torch.empty(B, H, N, device=q.device, dtype=torch.float32)
+        sparse_attn_cuda.forward(q, k, v, mask_packed, out, lse, scale, True, occupancy=occupancy)
     if orig_dtype == torch.float32:
         out = out.float()
     return out
