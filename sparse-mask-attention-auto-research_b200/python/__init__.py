@@ -6,5 +6,7 @@ from .sparse_attention import (
     sparse_attention,
     sparse_attention_func,
 )
+from .streaming import sparse_attention_from_host
 
-__all__ = ["sparse_attention", "sparse_attention_func", "pack_mask", "SparseAttentionFunction"]
+__all__ = ["sparse_attention", "sparse_attention_func", "pack_mask", "SparseAttentionFunction",
+           "sparse_attention_from_host"]
