@@ -5,7 +5,8 @@
 output [B, H, N, D] in pinned host memory.  The batch*head range crosses
 PCIe in contiguous slices on a copy-in stream; each slice is packed and
 attended on the current stream as soon as its inputs have landed, and its
-output goes back on a copy-out stream.  PCIe carries both directions at once
+output goes back on a copy-out stream, the slices shrinking along the range.
+PCIe carries both directions at once
 (on a B200 box: 88 MB in alone 1.600 ms, with a 12.6 MB read back at the same
 time 1.630 ms), so every slice's kernels and read-back except the last
 slice's hide under the input copies that follow them.
@@ -41,17 +42,30 @@ def _copy_streams(device):
     return s
 
 
-_SLICE_BYTES = 16 << 20  # input bytes per slice, about
+_SLICE_BYTES = 20 << 20  # input bytes per slice, on average
 _MAX_SLICES = 8
 
 
 def default_slices(bh, input_bytes):
     """Slices for `bh` heads whose inputs (q, k, v and the bool mask) take
-    `input_bytes`: about 16 MB each, at most 8, at most one per head.  On a
-    B200 box the best counts measured were 4 for 88 MB (B16 H12 N512 D64), 3
-    for 50 MB (B64 H12 N128) and 6-8 for 469 MB (B8 H32 N1024 D128); smaller
-    slices pay more per-copy and per-launch overhead than they hide."""
+    `input_bytes`: about 20 MB each on average, at most 8, at most one per
+    head.  On a B200 box the best counts measured were 4 for 88 MB (B16 H12
+    N512 D64) and 92 MB (B4 H16 N1024 D64, causal), 2-3 for 50 MB (B64 H12
+    N128) and 6-8 for 469 MB (B8 H32 N1024 D128); more, smaller slices pay
+    more per-copy and per-launch overhead than they hide."""
     return max(1, min(bh, _MAX_SLICES, input_bytes // _SLICE_BYTES))
+
+
+def slice_bounds(bh, slices):
+    """Bounds of `slices` contiguous parts of range(bh), in decreasing sizes
+    (weights slices, slices - 1, ..., 1): only the last part's kernels and
+    read-back are not hidden under later copies, so it is the smallest."""
+    total = slices * (slices + 1) // 2
+    bounds, acc = [0], 0
+    for i in range(slices):
+        acc += slices - i
+        bounds.append(bh * acc // total)
+    return bounds
 
 
 def sparse_attention_from_host(q, k, v, mask, slices=None, out=None):
@@ -105,7 +119,7 @@ def sparse_attention_from_host(q, k, v, mask, slices=None, out=None):
     start = torch.cuda.Event()
     start.record(cur)
     s_in.wait_event(start)
-    bounds = [BH * i // slices for i in range(slices + 1)]
+    bounds = slice_bounds(BH, slices)
     parts = [(bounds[i], bounds[i + 1]) for i in range(slices) if bounds[i + 1] > bounds[i]]
     # Every slice's input copies are queued first, so the copy engine never
     # waits on the host for the next one.

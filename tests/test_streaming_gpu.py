@@ -38,7 +38,7 @@ def test_c1_equals_device_api(slices):
 
 
 def test_bf16_head_dim_128_ragged_slices_and_out():
-    # 2 x 7 = 14 heads in 4 slices (3, 4, 3, 4 heads): every slice smaller than the GPU.
+    # 2 x 7 = 14 heads in 4 slices (5, 4, 3, 2 heads): every slice smaller than the GPU.
     (q, k, v, m), (hq, hk, hv, hm) = _host_inputs("c3", B=2, H=7, seed=1)
     out = torch.empty(hq.shape, dtype=hq.dtype).pin_memory()
     res = sparse_attention_from_host(hq, hk, hv, hm, slices=4, out=out)
