@@ -37,7 +37,7 @@ _DTYPES = {torch.float16: _lib.SMA_DTYPE_FP16, torch.bfloat16: _lib.SMA_DTYPE_BF
 
 
 # The current stream's handle without building a torch.cuda.Stream object
-# (0.1 against 2.3 us per call on a B200 box); the public call where torch
+# (0.1 against 2.3 us per call, measured on a B200 host); the public call where torch
 # lacks it.
 _raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
 

@@ -7,7 +7,7 @@ PCIe in contiguous slices on a copy-in stream; each slice is packed and
 attended on the current stream as soon as its inputs have landed, and its
 output goes back on a copy-out stream, the slices shrinking along the range.
 PCIe carries both directions at once
-(on a B200 box: 88 MB in alone 1.600 ms, with a 12.6 MB read back at the same
+(measured on a B200 host: 88 MB in alone 1.600 ms, with a 12.6 MB read back at the same
 time 1.630 ms), so every slice's kernels and read-back except the last
 slice's hide under the input copies that follow them.
 
@@ -49,7 +49,7 @@ _MAX_SLICES = 8
 def default_slices(bh, input_bytes):
     """Slices for `bh` heads whose inputs (q, k, v and the bool mask) take
     `input_bytes`: about 20 MB each on average, at most 8, at most one per
-    head.  On a B200 box the best counts measured were 4 for 88 MB (B16 H12
+    head.  On a B200 host the best counts measured were 4 for 88 MB (B16 H12
     N512 D64) and 92 MB (B4 H16 N1024 D64, causal), 2-3 for 50 MB (B64 H12
     N128) and 6-8 for 469 MB (B8 H32 N1024 D128); more, smaller slices pay
     more per-copy and per-launch overhead than they hide."""
